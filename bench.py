@@ -1,0 +1,411 @@
+"""Benchmark: dense-constant fold GB/s (in+out) on B200.
+
+Workload (one step): the 4096x4096 f32 fold chain — four dense constants
+A, B, C, D (uniform[-4,4), 0.5% exact zeros in the divisor) folded through
+addf, mulf, subf, divf, maximumf, minimumf: six elementwise folds of
+16,777,216 elements, 192 MiB of algorithmic traffic each (two 64 MiB
+operands in, one 64 MiB result out), 1.125 GiB per step.
+
+  value  GB/s of algorithmic bytes with the constants resident in HBM:
+         the six fold kernels launched through the device entry points,
+         each timed with CUDA events on its launch stream, L2 flushed
+         (256 MiB write) before every fold so each reads HBM;
+  e2e    the same bytes through the host C ABI (dcf_binary) from pinned
+         host buffers: every fold copies its two operands host->device and
+         its result device->host inside the timed region;
+  cpu_baseline  the oracle (the scalar C restatement of the reference's
+         fold loop, which runs single-threaded in the reference) timed on
+         this host on a bounded sample.
+
+Multi-GPU: one process per GPU (torchrun); each rank folds its own copy of
+the chain — one isolated function per GPU, no data-path collective — and
+`value` is the total bytes over the slowest rank's time (weak scaling).
+
+`--impl reference` times the reference's CPU fold path instead: the oracle
+port with all host threads (the reference cannot be built here: no Rust
+toolchain, and its arithmetic crate is not vendored).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SIDE = 4096
+N = SIDE * SIDE
+FOLD_BYTES = 3 * 4 * N                 # two f32 operands in, one f32 result out
+CHAIN = [("addf", "A", "B", "t1"), ("mulf", "t1", "C", "t2"), ("subf", "t2", "D", "t3"),
+         ("divf", "t3", "D", "t4"), ("maximumf", "t4", "A", "t5"), ("minimumf", "t5", "B", "t6")]
+STEP_BYTES = FOLD_BYTES * len(CHAIN)
+METRIC = "dense-constant fold GB/s (in+out)"
+CONFIG = {
+    "workload": "4x 4096x4096 f32 dense constants folded by the chain addf, mulf, subf, divf, maximumf, "
+                "minimumf under canonicalize (6 folds x 16,777,216 elements, 1.125 GiB algorithmic per step)",
+    "elements_per_fold": N,
+    "folds_per_step": len(CHAIN),
+    "bytes_per_step": STEP_BYTES,
+    "l2": "operands (256 MiB) exceed L2; L2 flushed with a 256 MiB write before every timed fold",
+    "unit_per_gpu": "one isolated function (the fold chain) per GPU",
+}
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch of the fold kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ew_binary_f32_chain4096.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus):
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_gpu(args):
+    import torch
+    import mlirpass_b200 as dcf
+    from mlirpass_b200 import workloads as W
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    os.environ["DCF_DEVICES"] = str(local)
+    dcf.init(1)
+    dev = torch.device("cuda", local)
+
+    d = W.config2(SIDE)
+    host = {k: d[k] for k in "ABCD"}
+    # device-resident operands and results
+    res = {k: torch.from_numpy(host[k]).to(dev) for k in "ABCD"}
+    for _, _, _, t in CHAIN:
+        res[t] = torch.empty(N, dtype=torch.float32, device=dev)
+    status = torch.empty(len(CHAIN) * 2, dtype=torch.int64, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def device_step(events=None):
+        for i, (op, a, b, t) in enumerate(CHAIN):
+            st = status[2 * i:2 * i + 2]
+            flush.zero_()
+            dcf.status_reset(st, stream)
+            if events is not None:
+                events[i][0].record(stream)
+            dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=N, stream=stream)
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    # correctness of the timed path: every fold folds, results not splat
+    for i in range(len(CHAIN)):
+        r = dcf.status_read(status[2 * i:2 * i + 2], stream)
+        if not r.folded:
+            raise SystemExit(f"fold {CHAIN[i][0]} refused at {r.first_fail_index}")
+
+    clocks = Clocks(local)
+    launches0 = dcf.kernel_launches()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in CHAIN] for _ in range(args.steps)]
+    for s in range(args.steps):
+        device_step(evs[s])
+    torch.cuda.synchronize()
+    barrier(world)
+    value_launches = dcf.kernel_launches() - launches0
+    fold_ms = [[evs[s][i][0].elapsed_time(evs[s][i][1]) for i in range(len(CHAIN))] for s in range(args.steps)]
+    step_ms = sum(sum(x) for x in fold_ms) / args.steps
+    kernel_ms = sum(sum(x) for x in fold_ms) / (args.steps * len(CHAIN))
+
+    # ---- e2e through the host C ABI, pinned host buffers
+    pin = {k: torch.from_numpy(host[k]).pin_memory() for k in "ABCD"}
+    for _, _, _, t in CHAIN:
+        pin[t] = torch.empty(N, dtype=torch.float32).pin_memory()
+    npv = {k: v.numpy() for k, v in pin.items()}
+
+    def host_step():
+        for op, a, b, t in CHAIN:
+            f = dcf.binary(op, "f32", npv[a], npv[b], out=npv[t].view(np.uint32))
+            if not f.folded:
+                raise SystemExit(f"e2e fold {op} refused")
+
+    for _ in range(max(1, args.warmup)):
+        host_step()
+    launches1 = dcf.kernel_launches()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_step()
+    e2e_s = time.perf_counter() - t0
+    barrier(world)
+    e2e_launches = dcf.kernel_launches() - launches1
+    clk = clocks.stop()
+
+    # bit-exact agreement of the two paths
+    same = all(torch.equal(res[t].cpu(), pin[t]) for _, _, _, t in CHAIN)
+
+    step_ms_max = allreduce_max(step_ms, world)
+    kernel_ms_max = allreduce_max(kernel_ms, world)
+    e2e_ms_max = allreduce_max(e2e_s * 1000.0 / args.steps, world)
+
+    if rank != 0:
+        return
+    peak, peak_kind = load_peaks()
+    gbs = world * STEP_BYTES / (step_ms_max * 1e-3) / 1e9
+    achieved = FOLD_BYTES / (kernel_ms_max * 1e-3) / 1e9
+    e2e_gbs = world * STEP_BYTES / (e2e_ms_max * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(gbs, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms_max, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (SplitMix64-seeded dense constants; no dataset)",
+        "config": dict(CONFIG, parallelism=f"{world} independent functions, one per GPU",
+                       results_bit_identical_device_vs_host_path=same),
+        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms_max, 3),
+                "h2d_bytes_per_step": 2 * 4 * N * len(CHAIN), "d2h_bytes_per_step": 4 * N * len(CHAIN),
+                "path": "dcf_binary (host C ABI), pinned host buffers, 6 calls per step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                     "kernel": "ew_kernel<FArith/FMinMax f32> (fused fold + refusal + splat test)",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s",
+                     "kernel_ms": round(kernel_ms_max, 5)},
+        "gpu_launches": int(value_launches + e2e_launches),
+        "gpu_launches_detail": {"value_path": int(value_launches), "e2e_path": int(e2e_launches)},
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(host, budget_s=args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(host, budget_s=12.0, threads=1):
+    """Time the oracle on the same chain: whole chains until `budget_s`."""
+    import oracle
+    from concurrent.futures import ThreadPoolExecutor
+
+    oracle.lib()
+    env = {k: host[k] for k in "ABCD"}
+    outs = {t: np.empty(N, dtype=np.uint32) for _, _, _, t in CHAIN}
+
+    def fold(op, a, b, t, lo, hi):
+        oracle.binary(op, "f32", env_v[a][lo:hi], env_v[b][lo:hi], out=outs[t][lo:hi])
+
+    env_v = {k: v.view(np.uint32) for k, v in env.items()}
+    for t in outs:
+        env_v[t] = outs[t]
+    bounds = [(N * i // threads, N * (i + 1) // threads) for i in range(threads)]
+    pool = ThreadPoolExecutor(threads) if threads > 1 else None
+    chains = 0
+    folds = 0
+    t0 = time.perf_counter()
+    while True:
+        for op, a, b, t in CHAIN:
+            if pool:
+                list(pool.map(lambda lh: fold(op, a, b, t, *lh), bounds))
+            else:
+                fold(op, a, b, t, 0, N)
+            folds += 1
+        chains += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    if pool:
+        pool.shutdown()
+    return {"value": round(folds * FOLD_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{chains} full chains ({folds} folds of 16,777,216 f32) of the same workload, "
+                      f"{dt:.1f} s, oracle C restatement (scalar, -O2)",
+            "seconds": round(dt, 2)}
+
+
+# ---------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world, rank, _ = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
+    if rank != 0:
+        return
+    from mlirpass_b200 import workloads as W
+    import oracle
+    from concurrent.futures import ThreadPoolExecutor
+
+    oracle.lib()
+    threads = os.cpu_count() or 1
+    d = W.config2(SIDE)
+    env = {k: d[k].view(np.uint32) for k in "ABCD"}
+    for _, _, _, t in CHAIN:
+        env[t] = np.empty(N, dtype=np.uint32)
+    bounds = [(N * i // threads, N * (i + 1) // threads) for i in range(threads)]
+    pool = ThreadPoolExecutor(threads)
+
+    def step():
+        for op, a, b, t in CHAIN:
+            list(pool.map(lambda lh: oracle.binary(op, "f32", env[a][lh[0]:lh[1]], env[b][lh[0]:lh[1]],
+                                                   out=env[t][lh[0]:lh[1]]), bounds))
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    ms = dt * 1000.0 / args.steps
+    gbs = STEP_BYTES / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64-seeded dense constants; no dataset)",
+        "config": dict(CONFIG, parallelism="host threads over row blocks (one process)"),
+        "impl": "reference",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "the full fold chain per step (the reference itself cannot be built here: "
+                                   "no Rust toolchain, mlirformat 0.9.0 not vendored), oracle C restatement "
+                                   f"on {threads} threads"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+        if env_int("WORLD_SIZE", 1) > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

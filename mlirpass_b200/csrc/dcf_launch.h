@@ -1,0 +1,71 @@
+// dcf_launch.h — internal launch interface between the host runtime and the
+// kernel translation units.  Not part of the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/dcfold.h"
+
+namespace dcf {
+
+// One job of a batched step, as the batch kernel reads it from device memory.
+struct BatchDesc {
+  const void* l;
+  const void* r;
+  void* o;
+  uint64_t n;
+  int lsplat;
+  int rsplat;
+  dcf_status* st;
+};
+
+struct EwLaunch {
+  int op = 0;
+  int dtype = 0;      // operand type
+  int out_dtype = 0;  // result type (convert ops); ignored otherwise
+  uint32_t flags = 0;
+  const void* l = nullptr;
+  const void* r = nullptr;
+  void* o = nullptr;
+  uint64_t n = 0;
+  const void* l0 = nullptr;
+  const void* r0 = nullptr;
+  int lsplat = 0;
+  int rsplat = 0;
+  uint64_t base = 0;
+  dcf_status* st = nullptr;
+  cudaStream_t stream = nullptr;
+  // batched form (n = the largest job's element count)
+  const BatchDesc* batch = nullptr;
+  int n_jobs = 0;
+};
+
+// Each returns DCF_OK, DCF_EUNSUPPORTED for an (op, type) pair it does not
+// handle, or DCF_ECUDA.
+int launch_float_binary(const EwLaunch& a);    // addf..minnumf, cmpf
+int launch_int_binary(const EwLaunch& a);      // addi..minui, cmpi
+int launch_convert(const EwLaunch& a);         // extf, truncf, si/uitofp, fptosi/ui
+int launch_reciprocal(const EwLaunch& a);
+
+int launch_transpose2d(size_t elem_size, uint64_t rows, uint64_t cols, const void* in, void* out,
+                       cudaStream_t stream);
+int launch_permute(size_t elem_size, int rank, const int64_t* in_shape, const int64_t* perms,
+                   const void* in, void* out, cudaStream_t stream);
+int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t stream);
+int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st, cudaStream_t stream);
+int launch_splat_check(const void* in, size_t elem_size, uint64_t n, dcf_status* st, cudaStream_t stream);
+
+// Count one kernel launch (dcf_kernel_launches).
+void note_launch();
+uint64_t launches();
+
+// Dispatch by op (used by the runtime).
+int launch_ew(const EwLaunch& a);
+
+size_t dtype_size(int dtype);
+bool is_float(int dtype);
+bool is_int(int dtype);
+
+}  // namespace dcf

@@ -1,0 +1,346 @@
+// dcf_misc.cu — dispatch, grid sizing, and the data-movement kernels:
+// transpose / permute (the layerwise transpose fold), the dense hex codec
+// (dense<"0x…"> bodies), and the splat test.
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+
+#include "dcf_kernels.cuh"
+
+namespace dcf {
+
+size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case DCF_I1: case DCF_I8: case DCF_F8E5M2: case DCF_F8E4M3: case DCF_F8E3M4: return 1;
+    case DCF_I16: case DCF_F16: case DCF_BF16: return 2;
+    case DCF_I32: case DCF_F32: return 4;
+    case DCF_I64: case DCF_F64: return 8;
+    default: return 0;
+  }
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launches() { return g_launches.load(std::memory_order_relaxed); }
+
+bool is_float(int dtype) { return dtype >= DCF_F16 && dtype <= DCF_F8E3M4; }
+bool is_int(int dtype) { return dtype >= DCF_I1 && dtype <= DCF_I64; }
+
+// Grid = min(blocks the work needs, blocks resident on all SMs at once).
+int grid_for(uint64_t work_items, const void* kernel) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> occ[64];
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    auto it = occ[dev].find(kernel);
+    if (it == occ[dev].end()) {
+      int b = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kThreads, 0) != cudaSuccess || b < 1) b = 1;
+      it = occ[dev].emplace(kernel, b).first;
+    }
+    per_sm = it->second;
+  }
+  const uint64_t resident = (uint64_t)sms[dev] * (uint64_t)per_sm;
+  uint64_t need = (work_items + (uint64_t)kThreads * kUnroll - 1) / ((uint64_t)kThreads * kUnroll);
+  if (need < 1) need = 1;
+  return (int)(need < resident ? need : resident);
+}
+
+int launch_ew(const EwLaunch& a) {
+  switch (a.op) {
+    case DCF_ADDF: case DCF_SUBF: case DCF_MULF: case DCF_DIVF:
+    case DCF_MAXIMUMF: case DCF_MINIMUMF: case DCF_MAXNUMF: case DCF_MINNUMF:
+    case DCF_CMPF:
+      return launch_float_binary(a);
+    case DCF_ADDI: case DCF_SUBI: case DCF_MULI: case DCF_ANDI: case DCF_ORI: case DCF_XORI:
+    case DCF_SHLI: case DCF_SHRUI: case DCF_SHRSI: case DCF_DIVSI: case DCF_DIVUI:
+    case DCF_REMSI: case DCF_REMUI: case DCF_MAXSI: case DCF_MAXUI: case DCF_MINSI: case DCF_MINUI:
+    case DCF_CMPI:
+      return launch_int_binary(a);
+    case DCF_EXTF: case DCF_TRUNCF: case DCF_SITOFP: case DCF_UITOFP: case DCF_FPTOSI: case DCF_FPTOUI:
+      return launch_convert(a);
+    case DCF_RECIPROCAL:
+      return launch_reciprocal(a);
+    default:
+      return DCF_EUNSUPPORTED;
+  }
+}
+
+// ------------------------------------------------------------ transpose
+
+// 2-byte elements, rows and cols multiples of 64: each 64x64 tile is read
+// as 32-bit column pairs of two adjacent rows, 2x2-transposed in registers,
+// and written to an XOR-swizzled 64x32-word shared tile, so that both the
+// global reads and the global writes are 128-byte coalesced rows and the
+// shared-memory accesses are free of bank conflicts.
+__global__ void __launch_bounds__(256) transpose_b16_kernel(const uint32_t* __restrict__ in,
+                                                            uint32_t* __restrict__ out, uint64_t rows,
+                                                            uint64_t cols) {
+  __shared__ uint32_t s[64][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t tiles_c = cols / 64, ntiles = (rows / 64) * tiles_c;
+  const uint64_t in_words = cols / 2, out_words = rows / 2;
+  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const uint64_t r0 = (t / tiles_c) * 64, c0 = (t % tiles_c) * 64;
+    uint32_t a[4], b[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int y = warp + 8 * k;
+      const uint64_t row = r0 + 2 * y;
+      a[k] = __ldg(in + row * in_words + c0 / 2 + lane);
+      b[k] = __ldg(in + (row + 1) * in_words + c0 / 2 + lane);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int y = warp + 8 * k;
+      const uint32_t w0 = (a[k] & 0xFFFFu) | (b[k] << 16);
+      const uint32_t w1 = (a[k] >> 16) | (b[k] & 0xFFFF0000u);
+      s[2 * lane][y ^ lane] = w0;
+      s[2 * lane + 1][y ^ lane] = w1;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int R = warp + 8 * k;
+      out[(c0 + R) * out_words + r0 / 2 + lane] = s[R][lane ^ (R >> 1)];
+    }
+    __syncthreads();
+  }
+}
+
+// Any element size and shape: classic 32x32 tile with a padded column.
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_any_kernel(const T* __restrict__ in, T* __restrict__ out,
+                                                            uint64_t rows, uint64_t cols) {
+  __shared__ T tile[32][33];
+  const uint64_t tiles_c = (cols + 31) / 32, ntiles = ((rows + 31) / 32) * tiles_c;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const uint64_t r0 = (t / tiles_c) * 32, c0 = (t % tiles_c) * 32;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint64_t r = r0 + ty + 8 * k, c = c0 + tx;
+      if (r < rows && c < cols) tile[ty + 8 * k][tx] = in[r * cols + c];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint64_t oc = c0 + ty + 8 * k, orr = r0 + tx;  // out row = input col
+      if (oc < cols && orr < rows) out[oc * rows + orr] = tile[tx][ty + 8 * k];
+    }
+    __syncthreads();
+  }
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 1;
+}
+
+int launch_transpose2d(size_t es, uint64_t rows, uint64_t cols, const void* in, void* out, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return DCF_OK;
+  const int sms = sm_count();
+  if (es == 2 && rows % 64 == 0 && cols % 64 == 0 && ((uintptr_t)in & 3) == 0 && ((uintptr_t)out & 3) == 0) {
+    const uint64_t nt = (rows / 64) * (cols / 64);
+    const uint64_t g = nt < (uint64_t)sms * 8 ? nt : (uint64_t)sms * 8;
+    note_launch();
+    transpose_b16_kernel<<<(unsigned)g, 256, 0, st>>>((const uint32_t*)in, (uint32_t*)out, rows, cols);
+  } else {
+    const uint64_t nt = ((rows + 31) / 32) * ((cols + 31) / 32);
+    const unsigned g = (unsigned)(nt < (uint64_t)sms * 8 ? nt : (uint64_t)sms * 8);
+    note_launch();
+    switch (es) {
+      case 1: transpose_any_kernel<uint8_t><<<g, 256, 0, st>>>((const uint8_t*)in, (uint8_t*)out, rows, cols); break;
+      case 2: transpose_any_kernel<uint16_t><<<g, 256, 0, st>>>((const uint16_t*)in, (uint16_t*)out, rows, cols); break;
+      case 4: transpose_any_kernel<uint32_t><<<g, 256, 0, st>>>((const uint32_t*)in, (uint32_t*)out, rows, cols); break;
+      case 8: transpose_any_kernel<uint64_t><<<g, 256, 0, st>>>((const uint64_t*)in, (uint64_t*)out, rows, cols); break;
+      default: return DCF_EINVAL;
+    }
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+struct PermDesc {
+  int rank;
+  int64_t out_shape[8];
+  int64_t src_stride[8];  // input stride of the dim that output dim i reads
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) permute_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t total,
+                                                      PermDesc d) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t o = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += stride) {
+    uint64_t rem = o, off = 0;
+    for (int i = d.rank - 1; i >= 0; i--) {
+      const uint64_t dim = (uint64_t)d.out_shape[i];
+      off += (rem % dim) * (uint64_t)d.src_stride[i];
+      rem /= dim;
+    }
+    out[o] = in[off];
+  }
+}
+
+int launch_permute(size_t es, int rank, const int64_t* in_shape, const int64_t* perms, const void* in, void* out,
+                   cudaStream_t st) {
+  if (rank < 1 || rank > 8) return DCF_EINVAL;
+  PermDesc d{};
+  d.rank = rank;
+  int64_t in_stride[8], total = 1;
+  for (int i = rank - 1; i >= 0; i--) {
+    if (in_shape[i] < 0) return DCF_EINVAL;
+    in_stride[i] = total;
+    total *= in_shape[i];
+  }
+  for (int i = 0; i < rank; i++) {
+    if (perms[i] < 0 || perms[i] >= rank) return DCF_EINVAL;
+    d.out_shape[i] = in_shape[perms[i]];
+    d.src_stride[i] = in_stride[perms[i]];
+  }
+  if (total == 0) return DCF_OK;
+  const int sms = sm_count();
+  const uint64_t need = ((uint64_t)total + 255) / 256;
+  const unsigned g = (unsigned)(need < (uint64_t)sms * 8 ? need : (uint64_t)sms * 8);
+  note_launch();
+  switch (es) {
+    case 1: permute_kernel<uint8_t><<<g, 256, 0, st>>>((const uint8_t*)in, (uint8_t*)out, total, d); break;
+    case 2: permute_kernel<uint16_t><<<g, 256, 0, st>>>((const uint16_t*)in, (uint16_t*)out, total, d); break;
+    case 4: permute_kernel<uint32_t><<<g, 256, 0, st>>>((const uint32_t*)in, (uint32_t*)out, total, d); break;
+    case 8: permute_kernel<uint64_t><<<g, 256, 0, st>>>((const uint64_t*)in, (uint64_t*)out, total, d); break;
+    default: return DCF_EINVAL;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+// ------------------------------------------------------------ hex codec
+
+__device__ __forceinline__ uint32_t hex2(uint32_t byte) {
+  const uint32_t hi = byte >> 4, lo = byte & 15;
+  const uint32_t ch = hi + 48 + (hi > 9 ? 7 : 0), cl = lo + 48 + (lo > 9 ? 7 : 0);
+  return ch | (cl << 8);
+}
+
+// 8 input bytes -> 16 characters per thread (vector path when aligned).
+__global__ void __launch_bounds__(256) hex_encode_kernel(const uint8_t* __restrict__ in, uint64_t nbytes,
+                                                         char* __restrict__ out, int vec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t nv = vec ? nbytes / 8 : 0;
+  for (uint64_t v = tid; v < nv; v += stride) {
+    const uint2 x = __ldg((const uint2*)(in + v * 8));
+    uint4 y;
+    y.x = hex2(x.x & 0xFF) | (hex2((x.x >> 8) & 0xFF) << 16);
+    y.y = hex2((x.x >> 16) & 0xFF) | (hex2(x.x >> 24) << 16);
+    y.z = hex2(x.y & 0xFF) | (hex2((x.y >> 8) & 0xFF) << 16);
+    y.w = hex2((x.y >> 16) & 0xFF) | (hex2(x.y >> 24) << 16);
+    *(uint4*)(out + v * 16) = y;
+  }
+  for (uint64_t i = nv * 8 + tid; i < nbytes; i += stride) {
+    const uint32_t h = hex2(in[i]);
+    out[2 * i] = (char)(h & 0xFF);
+    out[2 * i + 1] = (char)(h >> 8);
+  }
+}
+
+__device__ __forceinline__ int unhex(uint32_t c) {
+  if (c >= '0' && c <= '9') return (int)(c - '0');
+  if (c >= 'A' && c <= 'F') return (int)(c - 'A' + 10);
+  if (c >= 'a' && c <= 'f') return (int)(c - 'a' + 10);
+  return -1;
+}
+
+// 16 characters -> 8 bytes per thread; an invalid character records its
+// index as the status's first_fail.
+__global__ void __launch_bounds__(256) hex_decode_kernel(const char* __restrict__ in, uint64_t nbytes,
+                                                         uint8_t* __restrict__ out, dcf_status* st, int vec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t nv = vec ? nbytes / 8 : 0;
+  uint64_t bad = ~0ull;
+  for (uint64_t v = tid; v < nv; v += stride) {
+    const uint4 x = __ldg((const uint4*)(in + v * 16));
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    uint32_t o[2] = {0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const uint32_t word = w[k / 2];
+      const uint32_t c0 = (word >> ((k & 1) * 16)) & 0xFF, c1 = (word >> ((k & 1) * 16 + 8)) & 0xFF;
+      const int h = unhex(c0), l = unhex(c1);
+      if (h < 0 || l < 0) {
+        const uint64_t at = v * 16 + 2 * k + (h < 0 ? 0 : 1);
+        bad = at < bad ? at : bad;
+      }
+      o[k / 4] |= (uint32_t)((h << 4 | l) & 0xFF) << ((k & 3) * 8);
+    }
+    *(uint2*)(out + v * 8) = make_uint2(o[0], o[1]);
+  }
+  for (uint64_t i = nv * 8 + tid; i < nbytes; i += stride) {
+    const int h = unhex((uint8_t)in[2 * i]), l = unhex((uint8_t)in[2 * i + 1]);
+    if (h < 0 || l < 0) {
+      const uint64_t at = 2 * i + (h < 0 ? 0 : 1);
+      bad = at < bad ? at : bad;
+    }
+    out[i] = (uint8_t)((h << 4 | l) & 0xFF);
+  }
+  report(st, bad, false);
+}
+
+int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t st) {
+  if (nbytes == 0) return DCF_OK;
+  const int vec = (((uintptr_t)in & 7) == 0 && ((uintptr_t)out & 15) == 0);
+  const uint64_t need = (nbytes / 8 + 255) / 256 + 1;
+  const int sms = sm_count();
+  const unsigned g = (unsigned)(need < (uint64_t)sms * 8 ? need : (uint64_t)sms * 8);
+  note_launch();
+  hex_encode_kernel<<<g, 256, 0, st>>>((const uint8_t*)in, nbytes, out, vec);
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* status, cudaStream_t st) {
+  if (nchars & 1) return DCF_EPARSE;
+  const uint64_t nbytes = nchars / 2;
+  const int vec = (((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 7) == 0);
+  const uint64_t need = (nbytes / 8 + 255) / 256 + 1;
+  const int sms = sm_count();
+  const unsigned g = (unsigned)(need < (uint64_t)sms * 8 ? need : (uint64_t)sms * 8);
+  note_launch();
+  hex_decode_kernel<<<g, 256, 0, st>>>(in, nbytes, (uint8_t*)out, status, vec);
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+// ----------------------------------------------------------- splat test
+
+template <typename T>
+__global__ void __launch_bounds__(256) splat_kernel(const T* __restrict__ in, uint64_t n, dcf_status* st) {
+  const T first = in[0];
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  bool differ = false;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) differ |= (in[i] != first);
+  report(st, ~0ull, differ);
+}
+
+int launch_splat_check(const void* in, size_t es, uint64_t n, dcf_status* status, cudaStream_t st) {
+  if (n == 0) return DCF_OK;
+  const int sms = sm_count();
+  const uint64_t need = (n + 255) / 256;
+  const unsigned g = (unsigned)(need < (uint64_t)sms * 8 ? need : (uint64_t)sms * 8);
+  note_launch();
+  switch (es) {
+    case 1: splat_kernel<uint8_t><<<g, 256, 0, st>>>((const uint8_t*)in, n, status); break;
+    case 2: splat_kernel<uint16_t><<<g, 256, 0, st>>>((const uint16_t*)in, n, status); break;
+    case 4: splat_kernel<uint32_t><<<g, 256, 0, st>>>((const uint32_t*)in, n, status); break;
+    case 8: splat_kernel<uint64_t><<<g, 256, 0, st>>>((const uint64_t*)in, n, status); break;
+    default: return DCF_EINVAL;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+}  // namespace dcf

@@ -1,0 +1,103 @@
+"""Drive the reference's golden fold vectors through an engine.
+
+An engine is a module with the host API of mlirpass_b200 (binary, convert,
+reciprocal): the product library on a GPU, or the oracle on the CPU.  The
+prologue that mlirpass's hooks run before the element loop (poison,
+type / elements equality, the dense-cmpf filter, the splat-only tosa folds;
+src/patterns/arith/canonicalize.rs:203-217, 457-467 and
+src/patterns/tosa/canonicalize.rs:497-511, 596-605) is restated here so each
+case reaches the engine exactly when the reference would run its loop.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+VECTORS = os.path.join(HERE, "golden", "fold_vectors.json")
+
+STORAGE = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
+SIZE = {"i1": 1, "i8": 1, "i16": 2, "i32": 4, "i64": 8, "index": 8, "f16": 2, "bf16": 2, "f32": 4, "f64": 8,
+        "f8E5M2": 1, "f8E4M3": 1, "f8E3M4": 1}
+CANON = {"index": "i64"}
+
+
+def load_cases():
+    with open(VECTORS) as fh:
+        return json.load(fh)["cases"]
+
+
+def element_cases():
+    """Cases whose outcome is decided by the element loop (no shortcut)."""
+    return [c for c in load_cases() if c["shortcut"] is None]
+
+
+def case_id(c) -> str:
+    return f'{c["fixture"].split("__")[1]}:{c["func"]}:{c["pos"]}'
+
+
+def _arr(o):
+    dt = CANON.get(o["dtype"], o["dtype"])
+    return np.array([int(b, 16) for b in o["bits"]], dtype=STORAGE[SIZE[dt]]), dt
+
+
+def _int_prop(props, key, default=0):
+    v = props.get(key)
+    if v is None:
+        return default
+    return int(v.split(":")[0].strip())
+
+
+def run_case(c, eng):
+    """Returns ("not_folded", None) or ("folded", (splat, bits list))."""
+    name = c["op"]
+    dialect, op = name.split(".", 1)
+    ops = c["operands"]
+    res = c["result"]
+    rdt = CANON.get(res["dtype"], res["dtype"])
+    if dialect == "tosa":
+        a, dt = _arr(ops[0])
+        if op == "reciprocal":
+            if dt not in ("f16", "bf16", "f32", "f64") or not ops[0]["splat"]:
+                return "not_folded", None
+            f = eng.reciprocal(dt, a, n=1, splat=True)
+        else:
+            raise ValueError(op)
+        return ("folded", (True, [int(x) for x in f.out[:1]])) if f.folded else ("not_folded", None)
+    if op in ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui"):
+        a, dt = _arr(ops[0])
+        n = 1 if ops[0]["splat"] else len(a)
+        f = eng.convert(op, dt, rdt, a, n=n, splat=ops[0]["splat"])
+        if not f.folded:
+            return "not_folded", None
+        return "folded", (ops[0]["splat"], [int(x) for x in f.out[:n]])
+    # binary
+    (a, dt), (b, dt2) = _arr(ops[0]), _arr(ops[1])
+    if dt != dt2 or ops[0]["elements"] != ops[1]["elements"] or ops[0]["shape"] != ops[1]["shape"]:
+        return "not_folded", None
+    if op == "cmpf" and ops[0]["elements"]:
+        return "not_folded", None
+    pred = _int_prop(c["props"], "predicate")
+    mode = _int_prop(c["props"], "roundingmode")
+    fl = (mode & 7) | ((pred & 15) << 8)
+    ls, rs = ops[0]["splat"], ops[1]["splat"]
+    n = 1 if (ls and rs) else max(len(a), len(b))
+    f = eng.binary(op, dt, a, b, n=n, lhs_splat=ls, rhs_splat=rs, flags=fl)
+    if not f.folded:
+        return "not_folded", None
+    return "folded", (ls and rs, [int(x) for x in f.out[:n]])
+
+
+def check_case(c, eng):
+    status, got = run_case(c, eng)
+    exp = c["expected"]
+    assert status == exp["status"], f"{case_id(c)}: expected {exp['status']}, got {status}"
+    if status == "folded":
+        splat, bits = got
+        want = [int(x, 16) for x in exp["bits"]]
+        if exp["splat"]:
+            assert all(x == want[0] for x in bits), f"{case_id(c)}: {bits} != splat {want}"
+        else:
+            assert bits == want, f"{case_id(c)}: {[hex(x) for x in bits]} != {[hex(x) for x in want]}"

@@ -1,0 +1,319 @@
+"""The oracle against independent arithmetic (CPU): numpy's IEEE-754 float
+ops and casts, Python integers, exact rationals for the directed rounding
+modes, binascii for the hex codec, numpy for permutations.
+
+These pin the parts of the restatement that the reference's golden vectors
+do not reach (large arrays, subnormals, every integer width, bf16).
+"""
+import binascii
+from fractions import Fraction
+
+import numpy as np
+import pytest
+
+from mlirpass_b200.workloads import splitmix64
+
+rng = np.random.default_rng(1234)
+
+
+def rand_f32(n, special=True):
+    x = rng.standard_normal(n).astype(np.float32) * np.float32(100.0)
+    b = x.view(np.uint32).copy()
+    if special:
+        k = n // 16
+        idx = rng.choice(n, size=6 * k, replace=False)
+        b[idx[:k]] = 0x7F800000                    # +inf
+        b[idx[k:2 * k]] = 0xFF800000               # -inf
+        b[idx[2 * k:3 * k]] = rng.integers(1, 1 << 23, size=k, dtype=np.uint32)  # denormals
+        b[idx[3 * k:4 * k]] = 0                    # +0
+        b[idx[4 * k:5 * k]] = 0x80000000           # -0
+        b[idx[5 * k:6 * k]] = 0x7F7FFFFF           # max
+    return b.view(np.float32)
+
+
+def qnan_mask(bits, e, m):
+    expm = ((1 << e) - 1) << m
+    return ((bits & expm) == expm) & ((bits & ((1 << m) - 1)) != 0)
+
+
+@pytest.mark.parametrize("op", ["addf", "subf", "mulf", "divf"])
+def test_f32_arith_matches_numpy(op, oracle):
+    a, b = rand_f32(20000), rand_f32(20000)
+    with np.errstate(all="ignore"):
+        ref = {"addf": a + b, "subf": a - b, "mulf": a * b, "divf": a / b}[op]
+    f = oracle.binary(op, "f32", a, b)
+    assert f.folded
+    got = f.out.view(np.uint32)
+    refb = ref.view(np.uint32)
+    nan = np.isnan(ref)
+    assert np.array_equal(got[~nan], refb[~nan])
+    # invalid operations give the positive default quiet NaN
+    assert np.all(got[nan] == 0x7FC00000)
+    f2 = oracle.binary(op, "f32", a, b, flags=1 << 16)
+    assert np.all(f2.out.view(np.uint32)[nan] == 0xFFC00000)
+
+
+@pytest.mark.parametrize("op", ["addf", "subf", "mulf", "divf"])
+def test_f64_and_f16_arith_match_numpy(op, oracle):
+    with np.errstate(all="ignore"):
+        a = rng.standard_normal(5000) * 1e3
+        b = rng.standard_normal(5000) * 1e-3
+        b[::50] = 0.0
+        ref = {"addf": a + b, "subf": a - b, "mulf": a * b, "divf": a / b}[op]
+        f = oracle.binary(op, "f64", a, b)
+        assert np.array_equal(f.out.view(np.uint64), ref.view(np.uint64))
+        h1 = (rng.standard_normal(5000) * 30).astype(np.float16)
+        h2 = (rng.standard_normal(5000) * 30).astype(np.float16)
+        h2[::40] = np.float16(0)
+        hr = {"addf": h1 + h2, "subf": h1 - h2, "mulf": h1 * h2, "divf": h1 / h2}[op]
+        fh = oracle.binary(op, "f16", h1, h2)
+        hb = hr.view(np.uint16)
+        nan = np.isnan(hr)
+        assert np.array_equal(fh.out[~nan], hb[~nan])
+
+
+def bf16_round(x32):
+    u = x32.view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return r.astype(np.uint16)
+
+
+@pytest.mark.parametrize("op", ["addf", "mulf", "divf"])
+def test_bf16_arith_is_correctly_rounded(op, oracle):
+    a = bf16_round((rng.standard_normal(5000) * 10).astype(np.float32))
+    b = bf16_round((rng.standard_normal(5000) * 10).astype(np.float32))
+    af = (a.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    bf = (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    with np.errstate(all="ignore"):
+        exact = {"addf": af + bf, "mulf": af * bf, "divf": af / bf}[op]  # f64: exact or 53-bit
+    # round f64 -> f32 -> bf16 is safe here (no ties created at f32 for these magnitudes is not
+    # guaranteed), so round directly from the double with integer arithmetic.
+    want = []
+    for v in exact:
+        want.append(int(oracle.lib().dco_round_from_double(17, float(v))))
+    f = oracle.binary(op, "bf16", a, b)
+    assert [int(x) for x in f.out] == want
+
+
+def directed(q: Fraction, mode: str):
+    """Exact directed rounding of a rational to f32 (normal range only)."""
+    x = float(q)
+    f = np.float32(x)
+    fq = Fraction(float(f))
+    if fq == q:
+        return f
+    up = np.nextafter(f, np.float32(np.inf)) if fq < q else f
+    dn = f if fq < q else np.nextafter(f, np.float32(-np.inf))
+    if mode == "down":
+        return dn
+    if mode == "up":
+        return up
+    return dn if q > 0 else up   # toward zero
+
+
+@pytest.mark.parametrize("op", ["addf", "subf", "mulf", "divf"])
+@pytest.mark.parametrize("mode,code", [("down", 1), ("up", 2), ("zero", 3)])
+def test_f32_directed_rounding(op, mode, code, oracle):
+    a = (rng.standard_normal(400) * 10).astype(np.float32)
+    b = (rng.standard_normal(400) * 10).astype(np.float32)
+    f = oracle.binary(op, "f32", a, b, flags=code)
+    assert f.folded
+    for x, y, got in zip(a, b, f.out.view(np.float32)):
+        qa, qb = Fraction(float(x)), Fraction(float(y))
+        q = {"addf": qa + qb, "subf": qa - qb, "mulf": qa * qb, "divf": qa / qb}[op]
+        assert got == directed(q, mode), (op, mode, x, y)
+
+
+def test_nearest_away_refuses_inexact_only(oracle):
+    a = np.array([1.0, 1.0], np.float32)
+    b = np.array([2.0, 3.0], np.float32)
+    f = oracle.binary("addf", "f32", a, b, flags=4)
+    assert f.folded                        # both sums exact
+    a2 = np.array([1.0, 1.0000001], np.float32)
+    f2 = oracle.binary("mulf", "f32", a2, np.array([3.0, 3.0], np.float32), flags=4)
+    assert not f2.folded and f2.first_fail_index == 1
+
+
+def test_minmax_rules(oracle):
+    qnan, snan = 0x7FC00001, 0x7F800001
+    a = np.array([0x80000000, 0, qnan, 0x3F800000, snan, 0x3F800000], np.uint32)
+    b = np.array([0, 0x80000000, 0x3F800000, qnan, 0x3F800000, snan], np.uint32)
+    mx = oracle.binary("maximumf", "f32", a, b).out
+    mn = oracle.binary("minimumf", "f32", a, b).out
+    mxn = oracle.binary("maxnumf", "f32", a, b).out
+    assert list(mx) == [0, 0, qnan, qnan, snan | 0x400000, snan | 0x400000]
+    assert list(mn) == [0x80000000, 0x80000000, qnan, qnan, snan | 0x400000, snan | 0x400000]
+    # *numf: a quiet NaN loses to the number, a signalling one wins quieted
+    assert list(mxn) == [0, 0, 0x3F800000, 0x3F800000, snan | 0x400000, snan | 0x400000]
+
+
+WIDTHS = {"i8": (np.int8, 8), "i16": (np.int16, 16), "i32": (np.int32, 32), "i64": (np.int64, 64)}
+
+
+def ints(dt, n, seed):
+    t, w = WIDTHS[dt]
+    r = splitmix64(seed, n)
+    v = (r & np.uint64((1 << w) - 1)).astype(np.dtype(t).str.replace("i", "u")).view(t)
+    edge = np.array([np.iinfo(t).min, np.iinfo(t).max, -1, 0, 1], dtype=t)
+    v[::7] = edge[(np.arange(len(v[::7])) % 5)]
+    return v
+
+
+def py_int_op(op, a, b, w):
+    m = (1 << w) - 1
+    ua, ub = a & m, b & m
+    sa = ua - (1 << w) if ua >> (w - 1) else ua
+    sb = ub - (1 << w) if ub >> (w - 1) else ub
+    if op == "addi": return (ua + ub) & m
+    if op == "subi": return (ua - ub) & m
+    if op == "muli": return (ua * ub) & m
+    if op == "andi": return ua & ub
+    if op == "ori": return ua | ub
+    if op == "xori": return ua ^ ub
+    if op in ("shli", "shrui", "shrsi"):
+        if ub >= w: return None
+        if op == "shli": return (ua << ub) & m
+        if op == "shrui": return ua >> ub
+        return (sa >> ub) & m
+    if op == "divsi":
+        if ub == 0 or (sa == -(1 << (w - 1)) and sb == -1): return None
+        q = abs(sa) // abs(sb)
+        return (q if (sa < 0) == (sb < 0) else -q) & m
+    if op == "divui":
+        return None if ub == 0 else ua // ub
+    if op == "remsi":
+        if ub == 0: return None
+        r = abs(sa) % abs(sb)
+        return (r if sa >= 0 else -r) & m
+    if op == "remui":
+        return None if ub == 0 else ua % ub
+    if op == "maxsi": return ua if sa > sb else ub
+    if op == "minsi": return ua if sa < sb else ub
+    if op == "maxui": return max(ua, ub)
+    if op == "minui": return min(ua, ub)
+    raise ValueError(op)
+
+
+@pytest.mark.parametrize("dt", ["i8", "i16", "i32", "i64"])
+@pytest.mark.parametrize("op", ["addi", "subi", "muli", "andi", "ori", "xori", "shli", "shrui", "shrsi",
+                                "divsi", "divui", "remsi", "remui", "maxsi", "minsi", "maxui", "minui"])
+def test_int_ops_match_python(op, dt, oracle):
+    t, w = WIDTHS[dt]
+    a, b = ints(dt, 700, 11), ints(dt, 700, 12)
+    if op.startswith("sh"):
+        b = (np.abs(b.astype(np.int64)) % w).astype(t)
+    if op in ("divsi", "divui", "remsi", "remui"):
+        b = np.where(b == 0, t(3), b).astype(t)
+        if op == "divsi":
+            b = np.where((a == np.iinfo(t).min) & (b == -1), t(2), b).astype(t)
+    ua = [int(x) & ((1 << w) - 1) for x in a]
+    ub = [int(x) & ((1 << w) - 1) for x in b]
+    want = [py_int_op(op, x, y, w) for x, y in zip(ua, ub)]
+    assert all(v is not None for v in want)
+    f = oracle.binary(op, dt, a, b)
+    assert f.folded
+    assert [int(x) for x in f.out] == want
+
+
+@pytest.mark.parametrize("dt", ["i8", "i32", "i64"])
+def test_int_refusals(dt, oracle):
+    t, w = WIDTHS[dt]
+    a = np.array([5, np.iinfo(t).min, 7, 9], t)
+    b = np.array([1, -1, 2, 0], t)
+    f = oracle.binary("divsi", dt, a, b)
+    assert not f.folded and f.first_fail_index == 1       # INT_MIN / -1
+    f = oracle.binary("remsi", dt, a, b)
+    assert not f.folded and f.first_fail_index == 3       # only the zero divisor refuses
+    f = oracle.binary("remsi", dt, a[:3], b[:3])
+    assert f.folded and int(f.out[1]) == 0                # INT_MIN % -1 folds to 0
+    s = np.array([0, w - 1, w, 1], t)
+    f = oracle.binary("shli", dt, a, s)
+    assert not f.folded and f.first_fail_index == 2
+
+
+def test_conversions_match_numpy(oracle):
+    x = rand_f32(30000)
+    xb = x.view(np.uint32)
+    nan = np.isnan(x)
+    h = x.astype(np.float16)
+    exact16 = (h.astype(np.float32).view(np.uint32) == xb) & ~nan
+    for i in np.nonzero(exact16)[0][:3000]:
+        ok, r = oracle.float_convert_bits("f32", "f16", int(xb[i]))
+        assert ok and r == int(h.view(np.uint16)[i])
+    for i in np.nonzero(~exact16 & ~nan)[0][:3000]:
+        ok, _ = oracle.float_convert_bits("f32", "f16", int(xb[i]))
+        assert not ok
+    # bf16: representable iff the low 16 bits are zero
+    for b in [0x3F800000, 0x3F800001, 0x00010000, 0x00008000, 0x7F800000, 0x7FC00000, 0x7FA00000, 0x7FC00001]:
+        ok, r = oracle.float_convert_bits("f32", "bf16", b)
+        if b in (0x7FA00000,):
+            assert not ok                       # signalling NaN refuses
+        elif b & 0xFFFF:
+            assert not ok
+        else:
+            assert ok and r == b >> 16
+    # extf is always exact for non-NaN values
+    hv = np.arange(0, 65536, 7, dtype=np.uint16)
+    f = oracle.convert("extf", "f16", "f32", hv)
+    hf = hv.view(np.float16)
+    isn = np.isnan(hf)
+    quiet = (hv & 0x200) != 0
+    if np.all(~isn | quiet):
+        assert f.folded
+    ok_idx = ~isn
+    # refusals stop the fold at a signalling NaN; compare on a NaN-free slice
+    hv2 = hv[~isn]
+    f2 = oracle.convert("extf", "f16", "f32", hv2)
+    assert f2.folded
+    assert np.array_equal(f2.out.view(np.float32), hv2.view(np.float16).astype(np.float32))
+    del ok_idx
+
+
+def test_int_float_casts_match_numpy(oracle):
+    i32 = ints("i32", 20000, 5)
+    f = oracle.convert("sitofp", "i32", "f32", i32)
+    assert np.array_equal(f.out.view(np.float32), i32.astype(np.float32))
+    i64 = ints("i64", 20000, 6)
+    f = oracle.convert("sitofp", "i64", "f32", i64)
+    assert np.array_equal(f.out.view(np.float32), i64.astype(np.float32))
+    f = oracle.convert("sitofp", "i64", "f64", i64)
+    assert np.array_equal(f.out.view(np.float64), i64.astype(np.float64))
+    # non-f32 kinds round through f64 first (Rust `as f64`, then from_f64)
+    f = oracle.convert("sitofp", "i64", "f16", i64)
+    assert np.array_equal(f.out.view(np.float16), i64.astype(np.float64).astype(np.float16))
+    u = ints("i32", 20000, 7).view(np.uint32)
+    f = oracle.convert("uitofp", "i32", "f32", u)
+    assert np.array_equal(f.out.view(np.float32), u.astype(np.float32))
+    x = (rng.standard_normal(20000) * 1e6).astype(np.float32)
+    f = oracle.convert("fptosi", "f32", "i32", x)
+    assert f.folded
+    assert np.array_equal(f.out.view(np.int32), np.trunc(x).astype(np.int32))
+    bad = np.array([1.0, 2.5e9, 3.0], np.float32)
+    f = oracle.convert("fptosi", "f32", "i32", bad)
+    assert not f.folded and f.first_fail_index == 1
+    f = oracle.convert("fptoui", "f32", "i32", np.array([0.0, -0.5, -1.0], np.float32))
+    assert not f.folded and f.first_fail_index == 2      # -0.5 truncates to -0, allowed
+    f = oracle.convert("fptosi", "f32", "i8", np.array([127.9, -128.9, 128.0], np.float32))
+    assert not f.folded and f.first_fail_index == 2
+
+
+def test_reciprocal_and_splat(oracle):
+    x = rand_f32(5000, special=False)
+    f = oracle.reciprocal("f32", x)
+    with np.errstate(all="ignore"):
+        assert np.array_equal(f.out.view(np.float32), np.float32(1.0) / x)
+    assert oracle.splat_check(np.full(100, 7, np.uint32))
+    assert not oracle.splat_check(np.arange(100, dtype=np.uint32))
+    f = oracle.binary("addf", "f32", np.full(64, 1.0, np.float32), np.full(64, 2.0, np.float32))
+    assert f.folded and f.is_splat
+
+
+def test_hex_and_transpose(oracle):
+    data = bytes(rng.integers(0, 256, 4099, dtype=np.uint8))
+    enc = oracle.hex_encode(data)
+    assert enc == binascii.hexlify(data).upper()
+    assert oracle.hex_decode(enc) == data
+    assert oracle.hex_decode(enc.lower()) == data
+    x = rng.integers(0, 1 << 16, size=(3, 5, 7), dtype=np.uint16)
+    for perms in [(1, 0, 2), (2, 1, 0), (0, 2, 1), (2, 0, 1)]:
+        assert np.array_equal(oracle.transpose(x, x.shape, perms), np.transpose(x, perms))
