@@ -147,11 +147,14 @@ typedef struct dcf_result {
 
 /* Device-side status written by the *_async entry points.  Reset it to all
  * 0xFF bytes before a fold; afterwards `first_fail == UINT64_MAX` means
- * folded and `splat_word != 0` means all output elements are equal. */
+ * folded, `splat_word != 0` means all output elements are equal, and
+ * `error != 0xFFFFFFFF` means a kernel gave up a bounded wait on its own
+ * copies (the fold's output is then not valid; dcf_status_read reports
+ * DCF_ETIMEOUT). */
 typedef struct dcf_status {
   unsigned long long first_fail;
   unsigned int splat_word;
-  unsigned int reserved;
+  unsigned int error;
 } dcf_status;
 
 /* One job of a batched fold (dcf_batch): one elementwise fold of one

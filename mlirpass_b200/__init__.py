@@ -68,7 +68,7 @@ class Result(ctypes.Structure):
 
 
 class Status(ctypes.Structure):
-    _fields_ = [("first_fail", ctypes.c_uint64), ("splat_word", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+    _fields_ = [("first_fail", ctypes.c_uint64), ("splat_word", ctypes.c_uint32), ("error", ctypes.c_uint32)]
 
 
 class Job(ctypes.Structure):

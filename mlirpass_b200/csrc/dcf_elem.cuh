@@ -155,12 +155,20 @@ template <class L> __device__ __forceinline__ double to_f64(uint64_t b) {
 
 // ----------------------------------------------- float binary arithmetic
 
-// ApFloat add/sub/mul/div at nearest-even with the NaN rule.
-template <int OP, class L>
-__device__ __forceinline__ uint64_t arith_rn(uint64_t a, uint64_t b, uint64_t dnan) {
+// NaN result of an operation whose operands were a and b: the first NaN
+// operand quieted, else (an invalid operation) the default NaN.
+template <class L>
+__device__ __forceinline__ uint64_t nan_result(uint64_t a, uint64_t b, uint64_t dnan) {
   if (is_nan<L>(a)) return a | L::QUIET;
   if (is_nan<L>(b)) return b | L::QUIET;
-  uint64_t r;
+  return dnan;
+}
+
+// ApFloat add/sub/mul/div at nearest-even with the NaN rule.  The hardware
+// result is used unless it is NaN; only then are the operands examined (a
+// non-NaN result implies that neither operand was NaN).
+template <int OP, class L>
+__device__ __forceinline__ uint64_t arith_rn(uint64_t a, uint64_t b, uint64_t dnan) {
   if constexpr (L::B == 8) {
     const double x = __longlong_as_double((long long)a), y = __longlong_as_double((long long)b);
     double z;
@@ -168,7 +176,8 @@ __device__ __forceinline__ uint64_t arith_rn(uint64_t a, uint64_t b, uint64_t dn
     else if constexpr (OP == DCF_SUBF) z = __dsub_rn(x, y);
     else if constexpr (OP == DCF_MULF) z = __dmul_rn(x, y);
     else z = __ddiv_rn(x, y);
-    r = (uint64_t)__double_as_longlong(z);
+    if (z != z) return nan_result<L>(a, b, dnan);
+    return (uint64_t)__double_as_longlong(z);
   } else if constexpr (L::B == 4 || L::E + L::M == 15) {
     // f32 directly; f16 / bf16 through f32 (precision 24 >= 2p+2, so the
     // two roundings equal one correct rounding to the narrow kind).
@@ -178,8 +187,8 @@ __device__ __forceinline__ uint64_t arith_rn(uint64_t a, uint64_t b, uint64_t dn
     else if constexpr (OP == DCF_SUBF) z = __fsub_rn(x, y);
     else if constexpr (OP == DCF_MULF) z = __fmul_rn(x, y);
     else z = __fdiv_rn(x, y);
-    if (z != z) return dnan;
-    r = from_f32_rn<L>(z);
+    if (z != z) return nan_result<L>(a, b, dnan);
+    return from_f32_rn<L>(z);
   } else {
     // f8 kinds: exact in f32 too; round with the generic packer.
     const float x = __uint_as_float((uint32_t)convert_rn<L, F32L>(a));
@@ -189,10 +198,9 @@ __device__ __forceinline__ uint64_t arith_rn(uint64_t a, uint64_t b, uint64_t dn
     else if constexpr (OP == DCF_SUBF) z = __fsub_rn(x, y);
     else if constexpr (OP == DCF_MULF) z = __fmul_rn(x, y);
     else z = __fdiv_rn(x, y);
-    if (z != z) return dnan;
-    r = convert_rn<F32L, L>(__float_as_uint(z));
+    if (z != z || is_nan<L>(a) || is_nan<L>(b)) return nan_result<L>(a, b, dnan);
+    return convert_rn<F32L, L>(__float_as_uint(z));
   }
-  return is_nan<L>(r) ? dnan : r;
 }
 
 __device__ __forceinline__ uint32_t f32_next(uint32_t b, bool up) {

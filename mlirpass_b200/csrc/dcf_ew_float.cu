@@ -4,15 +4,23 @@
 
 namespace dcf {
 
-template <int OP, class L> struct FArith {
+// NEAREST: the roundingmode property is absent or nearest-even, the only
+// mode every fold config uses; the directed modes get their own kernels so
+// the common one carries none of their code.
+template <int OP, class L, bool NEAREST> struct FArith {
   using In = typename L::T;
   using Out = typename L::T;
   static constexpr bool kBinary = true;
   __device__ static __forceinline__ bool apply(In a, In b, uint32_t flags, Out& o) {
-    uint64_t r = 0;
-    const bool ok = rounded<OP, L>(a, b, (int)(flags & DCF_FLAG_ROUND_MASK), default_nan<L>(flags), r);
-    o = (Out)r;
-    return ok;
+    if constexpr (NEAREST) {
+      o = (Out)arith_rn<OP, L>(a, b, default_nan<L>(flags));
+      return true;
+    } else {
+      uint64_t r = 0;
+      const bool ok = rounded<OP, L>(a, b, (int)(flags & DCF_FLAG_ROUND_MASK), default_nan<L>(flags), r);
+      o = (Out)r;
+      return ok;
+    }
   }
 };
 
@@ -50,12 +58,17 @@ template <class L> struct FRecip {
   }
 };
 
+template <int OP, class L> static int arith_for(const EwLaunch& a) {
+  if ((a.flags & DCF_FLAG_ROUND_MASK) == 0) return launch_one<FArith<OP, L, true>>(a);
+  return launch_one<FArith<OP, L, false>>(a);
+}
+
 template <class L> static int float_binary_for(const EwLaunch& a) {
   switch (a.op) {
-    case DCF_ADDF: return launch_one<FArith<DCF_ADDF, L>>(a);
-    case DCF_SUBF: return launch_one<FArith<DCF_SUBF, L>>(a);
-    case DCF_MULF: return launch_one<FArith<DCF_MULF, L>>(a);
-    case DCF_DIVF: return launch_one<FArith<DCF_DIVF, L>>(a);
+    case DCF_ADDF: return arith_for<DCF_ADDF, L>(a);
+    case DCF_SUBF: return arith_for<DCF_SUBF, L>(a);
+    case DCF_MULF: return arith_for<DCF_MULF, L>(a);
+    case DCF_DIVF: return arith_for<DCF_DIVF, L>(a);
     case DCF_MAXIMUMF: return launch_one<FMinMax<L, true, true>>(a);
     case DCF_MINIMUMF: return launch_one<FMinMax<L, false, true>>(a);
     case DCF_MAXNUMF: return launch_one<FMinMax<L, true, false>>(a);

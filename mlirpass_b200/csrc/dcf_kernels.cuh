@@ -85,9 +85,55 @@ __device__ __forceinline__ bool apply2(const typename F::In& a, const typename F
 }
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 2;
+constexpr int kUnroll = 4;
+
+template <class F, int VEC>
+__device__ __forceinline__ void load_chunk(const typename F::In* __restrict__ l, const typename F::In* __restrict__ r,
+                                           uint64_t c, bool lsplat, bool rsplat, typename F::In a0,
+                                           typename F::In b0, typename F::In (&av)[VEC], typename F::In (&bv)[VEC]) {
+  using In = typename F::In;
+  if (lsplat) {
+#pragma unroll
+    for (int k = 0; k < VEC; k++) av[k] = a0;
+  } else if constexpr (VEC * sizeof(In) == 16) {
+    *(uint4*)av = __ldg((const uint4*)(l + c * VEC));
+  } else {
+    av[0] = l[c];
+  }
+  if constexpr (F::kBinary) {
+    if (rsplat) {
+#pragma unroll
+      for (int k = 0; k < VEC; k++) bv[k] = b0;
+    } else if constexpr (VEC * sizeof(In) == 16) {
+      *(uint4*)bv = __ldg((const uint4*)(r + c * VEC));
+    } else {
+      bv[0] = r[c];
+    }
+  }
+}
+
+template <class F, int VEC>
+__device__ __forceinline__ void fold_chunk(typename F::Out* __restrict__ o, uint64_t c, uint64_t base,
+                                           uint32_t flags, const typename F::In (&av)[VEC],
+                                           const typename F::In (&bv)[VEC], typename F::Out o0,
+                                           uint64_t& my_fail, bool& nonsplat) {
+  using In = typename F::In;
+  using Out = typename F::Out;
+  Out ov[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; k++) {
+    if (!apply2<F>(av[k], F::kBinary ? bv[k] : In(0), flags, ov[k])) {
+      const uint64_t idx = base + c * VEC + k;
+      my_fail = idx < my_fail ? idx : my_fail;
+    }
+    nonsplat |= (ov[k] != o0);
+  }
+  VecIO<int(VEC * sizeof(Out))>::st(o + c * VEC, ov);
+}
 
 // VECTOR: operand pointers are 16-byte aligned and VEC = 16 / sizeof(In).
+// The main loop issues kUnroll 16-byte loads per operand per thread before
+// any arithmetic, with no bounds tests; a final pass handles the ragged end.
 template <class F, bool VECTOR>
 __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
   using In = typename F::In;
@@ -97,6 +143,7 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
   const In* __restrict__ r = (const In*)p.r;
   Out* __restrict__ o = (Out*)p.o;
   const uint32_t flags = p.flags;
+  const bool lsplat = p.lsplat != 0, rsplat = p.rsplat != 0;
 
   const In a0 = *(const In*)p.l0;
   const In b0 = F::kBinary ? *(const In*)p.r0 : In(0);
@@ -109,56 +156,25 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
   const uint64_t stride = (uint64_t)gridDim.x * kThreads;
   const uint64_t tid = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
 
-  for (uint64_t c0 = tid; c0 < nvec; c0 += stride * kUnroll) {
+  uint64_t c0 = tid;
+  for (; c0 + (kUnroll - 1) * stride < nvec; c0 += kUnroll * stride) {
     In av[kUnroll][VEC], bv[kUnroll][VEC];
 #pragma unroll
-    for (int u = 0; u < kUnroll; u++) {
-      const uint64_t c = c0 + (uint64_t)u * stride;
-      if (c < nvec) {
-        if (p.lsplat) {
+    for (int u = 0; u < kUnroll; u++) load_chunk<F, VEC>(l, r, c0 + u * stride, lsplat, rsplat, a0, b0, av[u], bv[u]);
 #pragma unroll
-          for (int k = 0; k < VEC; k++) av[u][k] = a0;
-        } else if constexpr (VECTOR) {
-          *(uint4*)av[u] = __ldg((const uint4*)(l + c * VEC));
-        } else {
-          av[u][0] = l[c];
-        }
-        if constexpr (F::kBinary) {
-          if (p.rsplat) {
-#pragma unroll
-            for (int k = 0; k < VEC; k++) bv[u][k] = b0;
-          } else if constexpr (VECTOR) {
-            *(uint4*)bv[u] = __ldg((const uint4*)(r + c * VEC));
-          } else {
-            bv[u][0] = r[c];
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; u++) {
-      const uint64_t c = c0 + (uint64_t)u * stride;
-      if (c < nvec) {
-        Out ov[VEC];
-#pragma unroll
-        for (int k = 0; k < VEC; k++) {
-          const bool ok = apply2<F>(av[u][k], F::kBinary ? bv[u][k] : In(0), flags, ov[k]);
-          if (!ok) {
-            const uint64_t idx = p.base + c * VEC + k;
-            my_fail = idx < my_fail ? idx : my_fail;
-          }
-          nonsplat |= (ov[k] != o0);
-        }
-        VecIO<int(VEC * sizeof(Out))>::st(o + c * VEC, ov);
-      }
-    }
+    for (int u = 0; u < kUnroll; u++) fold_chunk<F, VEC>(o, c0 + u * stride, p.base, flags, av[u], bv[u], o0, my_fail, nonsplat);
+  }
+  for (; c0 < nvec; c0 += stride) {
+    In av[VEC], bv[VEC];
+    load_chunk<F, VEC>(l, r, c0, lsplat, rsplat, a0, b0, av, bv);
+    fold_chunk<F, VEC>(o, c0, p.base, flags, av, bv, o0, my_fail, nonsplat);
   }
   // Tail elements that do not fill a vector.
   const uint64_t tail0 = nvec * VEC;
   if (tid < p.n - tail0) {
     const uint64_t i = tail0 + tid;
-    const In a = p.lsplat ? a0 : l[i];
-    const In b = F::kBinary ? (p.rsplat ? b0 : r[i]) : In(0);
+    const In a = lsplat ? a0 : l[i];
+    const In b = F::kBinary ? (rsplat ? b0 : r[i]) : In(0);
     Out ov;
     if (!apply2<F>(a, b, flags, ov)) {
       const uint64_t idx = p.base + i;
@@ -166,6 +182,156 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
     }
     nonsplat |= (ov != o0);
     o[i] = ov;
+  }
+  report(p.st, my_fail, nonsplat);
+}
+
+// ----------------------------------------------------------------------
+// Bulk-copy (TMA) pipeline for large aligned folds.  Persistent CTAs; each
+// stage holds one 16 KB tile of every streamed operand, filled by one
+// cp.async.bulk per operand that completes on the stage's mbarrier.  All
+// 256 threads consume the stage from shared memory and store results
+// straight from registers; thread 0 refills the stage once every thread has
+// read it.  Waits are bounded: a CTA that waits too long records the fact
+// in the status's error word, drains its copies (again bounded) and exits.
+constexpr int kTileBytes = 16384;
+constexpr int kStages = 2;
+constexpr int kTmaCtasPerSm = 3;
+constexpr long kWaitLimit = 1l << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`; false when the bound ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  for (long spins = 0; !mbar_try_wait(bar, parity); spins++)
+    if (spins > kWaitLimit) return false;
+  return true;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+template <class F>
+__global__ void __launch_bounds__(kThreads) ew_tma_kernel(EwParams p) {
+  using In = typename F::In;
+  using Out = typename F::Out;
+  constexpr int VEC = int(16 / sizeof(In));
+  constexpr int TE = kTileBytes / int(sizeof(In));   // elements per tile
+  constexpr int TV = TE / VEC;                       // 16-byte chunks per tile
+  extern __shared__ __align__(128) uint8_t smem[];
+  const bool lsplat = p.lsplat != 0, rsplat = p.rsplat != 0;
+  const bool lcopy = !lsplat, rcopy = F::kBinary && !rsplat;
+  In* sl = (In*)smem;
+  In* sr = (In*)(smem + (lcopy ? kStages * kTileBytes : 0));
+  uint64_t* full = (uint64_t*)(smem + kStages * kTileBytes * ((lcopy ? 1 : 0) + (rcopy ? 1 : 0)));
+  const unsigned tx = (lcopy ? kTileBytes : 0) + (rcopy ? kTileBytes : 0);
+  const In* __restrict__ l = (const In*)p.l;
+  const In* __restrict__ r = (const In*)p.r;
+  Out* __restrict__ o = (Out*)p.o;
+  const uint32_t flags = p.flags;
+  const uint64_t ntiles = p.n / TE;
+
+  const In a0 = *(const In*)p.l0;
+  const In b0 = F::kBinary ? *(const In*)p.r0 : In(0);
+  Out o0;
+  apply2<F>(a0, b0, flags, o0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int s = 0; s < kStages; s++) {
+      const uint64_t t = blockIdx.x + (uint64_t)s * gridDim.x;
+      if (t < ntiles) {
+        mbar_expect_tx(&full[s], tx);
+        if (lcopy) bulk_load(sl + s * TE, l + t * TE, kTileBytes, &full[s]);
+        if (rcopy) bulk_load(sr + s * TE, r + t * TE, kTileBytes, &full[s]);
+      }
+    }
+  }
+  __syncthreads();
+
+  uint64_t my_fail = ~0ull;
+  bool nonsplat = false;
+  uint64_t i = 0;
+  bool dead = false;
+  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+    const int s = (int)(i % kStages);
+    const bool ok = mbar_wait_bounded(&full[s], (unsigned)((i / kStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      dead = true;
+      break;
+    }
+#pragma unroll
+    for (int k = threadIdx.x; k < TV; k += kThreads) {
+      In av[VEC], bv[VEC];
+      if (lsplat) {
+#pragma unroll
+        for (int e = 0; e < VEC; e++) av[e] = a0;
+      } else {
+        *(uint4*)av = *(const uint4*)(sl + s * TE + k * VEC);
+      }
+      if constexpr (F::kBinary) {
+        if (rsplat) {
+#pragma unroll
+          for (int e = 0; e < VEC; e++) bv[e] = b0;
+        } else {
+          *(uint4*)bv = *(const uint4*)(sr + s * TE + k * VEC);
+        }
+      }
+      fold_chunk<F, VEC>(o, t * TV + k, p.base, flags, av, bv, o0, my_fail, nonsplat);
+    }
+    __syncthreads();  // every thread has read stage s
+    if (threadIdx.x == 0) {
+      const uint64_t tn = t + (uint64_t)kStages * gridDim.x;
+      if (tn < ntiles) {
+        mbar_expect_tx(&full[s], tx);
+        if (lcopy) bulk_load(sl + s * TE, l + tn * TE, kTileBytes, &full[s]);
+        if (rcopy) bulk_load(sr + s * TE, r + tn * TE, kTileBytes, &full[s]);
+      }
+    }
+  }
+  if (dead) {
+    // Drain the fills still in flight (bounded) before the CTA exits.
+    for (uint64_t j = i; j < i + kStages; j++) {
+      if (blockIdx.x + j * gridDim.x >= ntiles) break;
+      mbar_wait_bounded(&full[j % kStages], (unsigned)((j / kStages) & 1));
+    }
+    if (threadIdx.x == 0) atomicExch(&p.st->error, 1u);
+    return;
+  }
+  // Elements past the last whole tile: plain loads, all CTAs.
+  const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+  for (uint64_t k = ntiles * TE + (uint64_t)blockIdx.x * kThreads + threadIdx.x; k < p.n; k += stride) {
+    const In a = lsplat ? a0 : l[k];
+    const In b = F::kBinary ? (rsplat ? b0 : r[k]) : In(0);
+    Out ov;
+    if (!apply2<F>(a, b, flags, ov)) {
+      const uint64_t idx = p.base + k;
+      my_fail = idx < my_fail ? idx : my_fail;
+    }
+    nonsplat |= (ov != o0);
+    o[k] = ov;
   }
   report(p.st, my_fail, nonsplat);
 }
@@ -248,6 +414,8 @@ __global__ void __launch_bounds__(kThreads) ew_batch_kernel(const BatchDesc* __r
 }
 
 int grid_for(uint64_t work_items, const void* kernel);
+int sm_count_current();
+bool prepare_smem(const void* kernel, int bytes);
 
 template <class F>
 int launch_one(const EwLaunch& a) {
@@ -267,6 +435,16 @@ int launch_one(const EwLaunch& a) {
                 (unsigned)a.n_jobs);
       ew_batch_kernel<F, false><<<grid, kThreads, 0, a.stream>>>(a.batch, a.flags);
     }
+    return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+  }
+  const int streamed = (a.lsplat ? 0 : 1) + (F::kBinary && !a.rsplat ? 1 : 0);
+  const uint64_t ntiles = a.n / (kTileBytes / sizeof(typename F::In));
+  const int sms = sm_count_current();
+  if (vec && streamed > 0 && ntiles >= (uint64_t)sms * 2) {
+    const int smem = kStages * kTileBytes * streamed + kStages * 8;
+    if (!prepare_smem((const void*)ew_tma_kernel<F>, smem)) return DCF_ECUDA;
+    const uint64_t g = ntiles < (uint64_t)sms * kTmaCtasPerSm ? ntiles : (uint64_t)sms * kTmaCtasPerSm;
+    ew_tma_kernel<F><<<(unsigned)g, kThreads, smem, a.stream>>>(p);
   } else if (vec) {
     const uint64_t items = a.n / (16 / sizeof(typename F::In));
     ew_kernel<F, true><<<grid_for(items, (const void*)ew_kernel<F, true>), kThreads, 0, a.stream>>>(p);

@@ -52,6 +52,34 @@ int grid_for(uint64_t work_items, const void* kernel) {
   return (int)(need < resident ? need : resident);
 }
 
+int sm_count_current() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (!sms[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 1;
+  }
+  return sms[dev];
+}
+
+// Raise a kernel's dynamic shared memory limit once per device.
+bool prepare_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = done[dev].find(kernel);
+  if (it != done[dev].end() && it->second >= bytes) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  done[dev][kernel] = bytes;
+  return true;
+}
+
 int launch_ew(const EwLaunch& a) {
   switch (a.op) {
     case DCF_ADDF: case DCF_SUBF: case DCF_MULF: case DCF_DIVF:

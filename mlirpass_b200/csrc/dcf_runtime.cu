@@ -90,7 +90,7 @@ struct Dev {
   void* d[2][3] = {{nullptr}};  // per slot: lhs, rhs, out chunk buffers
   void* h[2][3] = {{nullptr}};  // per slot: pinned staging
   dcf_status* st = nullptr;
-  void* d0 = nullptr;           // 16 bytes: lhs element 0, rhs element 0
+  void* d0 = nullptr;           // 32 bytes: lhs element 0 at +0, rhs element 0 at +16
   void* big[3] = {nullptr};     // whole-tensor buffers (transpose, batch)
   size_t big_cap[3] = {0};
   void* hbig = nullptr;         // pinned whole-batch staging
@@ -114,7 +114,7 @@ int dev_setup(Dev& d) {
   }
   CK(cudaEventCreateWithFlags(&d.start, cudaEventDisableTiming));
   CK(cudaMalloc((void**)&d.st, sizeof(dcf_status)));
-  CK(cudaMalloc(&d.d0, 16));
+  CK(cudaMalloc(&d.d0, 32));
   return DCF_OK;
 }
 
@@ -279,7 +279,10 @@ int ensure_big(Dev& d, int j, size_t bytes) {
 int read_status(Dev& d, cudaStream_t s, dcf_status* out) {
   CK(cudaMemcpyAsync(out, d.st, sizeof(dcf_status), cudaMemcpyDeviceToHost, s));
   CK(cudaEventRecord(d.ev[0], s));
-  return wait_event(d.ev[0]);
+  int rc = wait_event(d.ev[0]);
+  if (rc) return rc;
+  if (out->error != 0xFFFFFFFFu) return set_err(DCF_ETIMEOUT, "a fold kernel gave up waiting for its own copies");
+  return DCF_OK;
 }
 
 struct EwJob {
@@ -301,7 +304,7 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
   cudaStream_t s0 = d.s[0], s1 = d.s[1];
   CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), s0));
   CK(cudaMemcpyAsync(d.d0, j.l, j.ies, cudaMemcpyHostToDevice, s0));
-  if (j.binary) CK(cudaMemcpyAsync((char*)d.d0 + 8, j.r, j.ies, cudaMemcpyHostToDevice, s0));
+  if (j.binary) CK(cudaMemcpyAsync((char*)d.d0 + 16, j.r, j.ies, cudaMemcpyHostToDevice, s0));
   CK(cudaEventRecord(d.start, s0));
   CK(cudaStreamWaitEvent(s1, d.start, 0));
 
@@ -326,7 +329,7 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
       }
     }
     const void* ldev = d.d0;
-    const void* rdev = (char*)d.d0 + 8;
+    const void* rdev = (char*)d.d0 + 16;
     if (!j.lsplat) {
       const void* src = (const char*)j.l + off * j.ies;
       if (!lp) {
@@ -355,7 +358,7 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
     a.o = d.d[k][2];
     a.n = cnt;
     a.l0 = d.d0;
-    a.r0 = (char*)d.d0 + 8;
+    a.r0 = (char*)d.d0 + 16;
     a.lsplat = j.lsplat;
     a.rsplat = j.rsplat;
     a.base = off;
@@ -681,6 +684,7 @@ int dcf_batch(dcf_job* jobs, size_t n_jobs) {
     memset(&j.result, 0, sizeof j.result);
     j.result.first_fail_index = UINT64_MAX;
     const bool bin = binary_op(j.op);
+    if (j.n == 0) j.result.folded = 1, j.result.is_splat = 1;
     if (bin) rc = check_binary(j.op, j.dtype);
     else if (convert_op(j.op)) rc = check_convert(j.op, j.dtype, j.out_dtype);
     else if (j.op == DCF_RECIPROCAL) rc = is_float(j.dtype) ? 0 : set_err(DCF_EINVAL, "reciprocal dtype");
@@ -691,8 +695,10 @@ int dcf_batch(dcf_job* jobs, size_t n_jobs) {
     if (bin && j.op != DCF_CMPI && j.op != DCF_CMPF) j.out_dtype = j.dtype;
     if (j.n && (!j.lhs || !j.out || (bin && !j.rhs))) return set_err(DCF_EINVAL, "job %zu: null buffer", i);
   }
-  std::vector<size_t> order(n_jobs);
-  for (size_t i = 0; i < n_jobs; i++) order[i] = i;
+  std::vector<size_t> order;
+  for (size_t i = 0; i < n_jobs; i++)
+    if (jobs[i].n) order.push_back(i);
+  n_jobs = order.size();
   auto key = [&](size_t i) {
     const dcf_job& j = jobs[i];
     return std::make_tuple(j.op, j.dtype, j.out_dtype, j.flags);
@@ -957,6 +963,7 @@ int dcf_status_read(const dcf_status* status, void* stream, dcf_result* res) {
   CK(cudaMemcpyAsync(&h, status, sizeof h, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
   CK(cudaStreamSynchronize((cudaStream_t)stream));
   memset(res, 0, sizeof *res);
+  if (h.error != 0xFFFFFFFFu) return set_err(DCF_ETIMEOUT, "a fold kernel gave up waiting for its own copies");
   res->first_fail_index = h.first_fail;
   res->folded = h.first_fail == ~0ull;
   res->is_splat = res->folded && h.splat_word != 0;

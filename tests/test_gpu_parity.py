@@ -289,3 +289,43 @@ def test_host_pinned_and_pageable_agree(dcf, oracle):
     f3 = oracle.binary("mulf", "f32", a.numpy(), b.numpy())
     same(f1, f3, n)
     same(f2, f3, n)
+
+
+TMA_CASES = [("binary", "addf", "f32", None), ("binary", "maximumf", "f32", None), ("binary", "mulf", "f64", None),
+             ("binary", "divsi", "i32", None), ("binary", "addi", "i8", None), ("binary", "cmpf", "f32", 4 << 8),
+             ("binary", "minnumf", "bf16", None), ("convert", "extf", "bf16", "f32"), ("convert", "sitofp", "i8", "f64"),
+             ("convert", "truncf", "f32", "f16"), ("convert", "fptosi", "f64", "i16")]
+
+
+@pytest.mark.parametrize("kind,op,dt,extra", TMA_CASES, ids=[f"{c[1]}-{c[2]}" for c in TMA_CASES])
+def test_bulk_copy_path_vs_oracle(kind, op, dt, extra, dcf, oracle):
+    """Large enough for the cp.async.bulk pipeline (>= 2 tiles of 16 KB per
+    SM), with a ragged tail that is not a whole tile or vector."""
+    n = (16384 // SZ[dt]) * 300 + 12345
+    if kind == "binary":
+        fl = extra or 0
+        a, b = rbits(dt, n, 71, "nonan"), rbits(dt, n, 72, "nonan")
+        if op == "divsi":
+            b = np.where(b == 0, b.dtype.type(3), b)
+        same(dcf.binary(op, dt, a, b, flags=fl), oracle.binary(op, dt, a, b, flags=fl), n)
+        s = rbits(dt, 1, 73, "nonan")
+        if op == "divsi":
+            s[:] = 7
+        same(dcf.binary(op, dt, a, s, rhs_splat=True, flags=fl), oracle.binary(op, dt, a, s, rhs_splat=True, flags=fl), n)
+        same(dcf.binary(op, dt, s, b, lhs_splat=True, n=n, flags=fl),
+             oracle.binary(op, dt, s, b, lhs_splat=True, n=n, flags=fl), n)
+        if op == "divsi":   # a refusal deep inside the tiled range, another in the tail
+            b2 = b.copy()
+            mid = n // 2 + 1
+            b2[n - 5] = 0
+            b2[mid] = 0
+            g, c = dcf.binary(op, dt, a, b2), oracle.binary(op, dt, a, b2)
+            assert not c.folded and c.first_fail_index == mid
+            same(g, c, n)
+    else:
+        x = rbits(dt, n, 74, "nonan")
+        if op == "truncf":
+            x = oracle.convert("extf", "f16", "f32", rbits("f16", n, 75, "nonan")).out
+        if op == "fptosi":
+            x = oracle.convert("sitofp", "i16", "f64", rbits("i16", n, 76)).out
+        same(dcf.convert(op, dt, extra, x), oracle.convert(op, dt, extra, x), n)
