@@ -259,6 +259,23 @@ int dcf_splat_check(const void* in, size_t elem_size, uint64_t n,
  * src/pass.rs:280-341 for the fold-only work of each function. */
 int dcf_batch(dcf_job* jobs, size_t n_jobs);
 
+/* As dcf_batch, but the jobs' lhs / rhs / out are DEVICE pointers (all on
+ * one device) and the call allocates no memory at all: no cudaMalloc, no
+ * cudaFree, no pinned or host heap.  No counterpart in the reference.  It
+ * is for callers that cannot allocate device memory when they fold: an
+ * embedding runtime whose caching allocator already holds all of HBM (a
+ * cudaMalloc would fail or fragment it), or latency-sensitive code that
+ * cannot take the device-wide synchronisation cudaMalloc / cudaFree may
+ * cause.  Its scratch (one descriptor and one status per job) is a fixed
+ * file-scope device array of 64 KiB, so a call takes at most 1024 jobs and
+ * a larger list is rejected with DCF_EINVAL.  The first call on a device
+ * looks up that array's device address (cudaGetSymbolAddress).  All calls
+ * share the array and each re-initialises what it uses; calls whose work
+ * overlaps on the GPU (from two threads or streams at once) race on it and
+ * must be serialised by the caller.  Work runs on `stream`; the call
+ * returns when its results are in each job's `result`. */
+int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream);
+
 /* ---- device entry points (caller-owned device memory, async) -------- */
 
 /* Fill a device dcf_status with 0xFF bytes on `stream`. */

@@ -97,6 +97,7 @@ SIGNATURES = {
     "dcf_hex_decode": (_I, [_VP, _U64, _VP]),
     "dcf_splat_check": (_I, [_VP, _SZ, _U64, ctypes.POINTER(ctypes.c_int)]),
     "dcf_batch": (_I, [ctypes.POINTER(Job), _SZ]),
+    "dcf_batch_noalloc": (_I, [ctypes.POINTER(Job), _SZ, _VP]),
     "dcf_status_reset_async": (_I, [_VP, _VP]),
     "dcf_binary_async": (_I, [_I, _I, _VP, _I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
     "dcf_convert_async": (_I, [_I, _I, _I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
@@ -284,6 +285,35 @@ def batch(jobs: list[dict]) -> list[Fold]:
 
 
 # ------------------------------------------------------------------ device
+
+NOALLOC_MAX_JOBS = 1024
+
+
+def batch_noalloc(jobs: list[dict], stream=None) -> list[Fold]:
+    """dcf_batch_noalloc: folds on device tensors with no allocation at all.
+
+    For callers that cannot allocate device memory while they fold (their
+    allocator owns all of HBM, or they cannot afford the synchronisation of
+    cudaMalloc).  Each job dict: op, dtype, [out_dtype], lhs, [rhs], out
+    (torch CUDA tensors on one device), [lhs_splat], [rhs_splat], [n],
+    [flags].  At most NOALLOC_MAX_JOBS jobs per call; overlapping calls on
+    the GPU race on the library's one scratch array.
+    """
+    arr = (Job * len(jobs))()
+    for i, j in enumerate(jobs):
+        op, dt = j["op"], j["dtype"]
+        odt = j.get("out_dtype") or ("i1" if op in ("cmpi", "cmpf") else dt)
+        arr[i].op, arr[i].dtype, arr[i].out_dtype = OPS[op], DTYPES[dt], DTYPES[odt]
+        arr[i].flags = j.get("flags", 0)
+        arr[i].lhs = _tptr(j["lhs"])
+        arr[i].rhs = _tptr(j["rhs"]) if "rhs" in j else None
+        arr[i].out = _tptr(j["out"])
+        arr[i].n = j.get("n") or j["out"].numel()
+        arr[i].lhs_splat = int(j.get("lhs_splat", False))
+        arr[i].rhs_splat = int(j.get("rhs_splat", False))
+    _check(lib().dcf_batch_noalloc(arr, len(jobs), _stream(stream)))
+    return [Fold(bool(arr[i].result.folded), bool(arr[i].result.is_splat), int(arr[i].result.first_fail_index),
+                 None) for i in range(len(jobs))]
 
 def _tptr(t) -> int:
     return t.data_ptr()

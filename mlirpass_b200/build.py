@@ -23,7 +23,7 @@ LIB = os.path.join(PKG, "libdcfold.so")
 ORACLE_SRC = os.path.join(ROOT, "oracle", "dcf_oracle.c")
 ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libdcforacle.so")
 
-SOURCES = ["dcf_ew_float.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_misc.cu", "dcf_runtime.cu"]
+SOURCES = ["dcf_ew_float.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_misc.cu", "dcf_runtime.cu", "dcf_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -57,6 +57,9 @@ int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t s
 int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st, cudaStream_t stream);
 int launch_splat_check(const void* in, size_t elem_size, uint64_t n, dcf_status* st, cudaStream_t stream);
 
+// Set the per-thread text dcf_last_error() returns; returns `code`.
+int record_error(int code, const char* msg);
+
 // Count one kernel launch (dcf_kernel_launches).
 void note_launch();
 uint64_t launches();

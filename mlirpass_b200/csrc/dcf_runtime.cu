@@ -38,6 +38,15 @@ namespace {
 
 thread_local std::string g_err;
 
+}  // namespace
+
+int dcf::record_error(int code, const char* msg) {
+  g_err = msg;
+  return code;
+}
+
+namespace {
+
 int set_err(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
