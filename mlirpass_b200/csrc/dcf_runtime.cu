@@ -65,8 +65,10 @@ int set_err(int code, const char* fmt, ...) {
                      __LINE__);                                                                    \
   } while (0)
 
-constexpr size_t kChunkBytes = 32ull << 20;  // per operand per slot
+constexpr size_t kChunkBytes = 32ull << 20;  // per operand per slot (whole-tensor staging)
 constexpr uint64_t kAlignElems = 64;         // row-block / chunk granularity
+constexpr int kPipeSlots = 4;                // elementwise pipeline depth
+constexpr size_t kPipeChunk = 8ull << 20;    // bytes of the widest operand per pipeline chunk
 
 long timeout_ms() {
   static long t = [] {
@@ -104,6 +106,13 @@ struct Dev {
   size_t big_cap[3] = {0};
   void* hbig = nullptr;         // pinned whole-batch staging
   size_t hbig_cap = 0;
+  // Elementwise pipeline: copy-in, compute and copy-out streams, with
+  // kPipeSlots rotating chunk buffers (lhs, rhs, out) and one event per
+  // slot and stage.
+  cudaStream_t sin = nullptr, scomp = nullptr, sout = nullptr;
+  cudaEvent_t evin[kPipeSlots] = {nullptr}, evcomp[kPipeSlots] = {nullptr}, evout[kPipeSlots] = {nullptr};
+  void* pd[kPipeSlots][3] = {{nullptr}};
+  void* ph[kPipeSlots][3] = {{nullptr}};
   std::mutex mu;
 };
 
@@ -122,6 +131,18 @@ int dev_setup(Dev& d) {
     }
   }
   CK(cudaEventCreateWithFlags(&d.start, cudaEventDisableTiming));
+  CK(cudaStreamCreateWithFlags(&d.sin, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&d.scomp, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&d.sout, cudaStreamNonBlocking));
+  for (int k = 0; k < kPipeSlots; k++) {
+    CK(cudaEventCreateWithFlags(&d.evin[k], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&d.evcomp[k], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&d.evout[k], cudaEventDisableTiming));
+    for (int j = 0; j < 3; j++) {
+      CK(cudaMalloc(&d.pd[k][j], kPipeChunk));
+      CK(cudaHostAlloc(&d.ph[k][j], kPipeChunk, cudaHostAllocPortable));
+    }
+  }
   CK(cudaMalloc((void**)&d.st, sizeof(dcf_status)));
   CK(cudaMalloc(&d.d0, 32));
   return DCF_OK;
@@ -139,6 +160,18 @@ void dev_free(Dev& d) {
     if (d.s[k]) cudaStreamDestroy(d.s[k]);
   }
   if (d.start) cudaEventDestroy(d.start);
+  for (cudaStream_t x : {d.sin, d.scomp, d.sout})
+    if (x) cudaStreamSynchronize(x);
+  for (int k = 0; k < kPipeSlots; k++) {
+    for (int j = 0; j < 3; j++) {
+      if (d.pd[k][j]) cudaFree(d.pd[k][j]);
+      if (d.ph[k][j]) cudaFreeHost(d.ph[k][j]);
+    }
+    for (cudaEvent_t e : {d.evin[k], d.evcomp[k], d.evout[k]})
+      if (e) cudaEventDestroy(e);
+  }
+  for (cudaStream_t x : {d.sin, d.scomp, d.sout})
+    if (x) cudaStreamDestroy(x);
   for (int j = 0; j < 3; j++)
     if (d.big[j]) cudaFree(d.big[j]);
   if (d.hbig) cudaFreeHost(d.hbig);
@@ -307,34 +340,48 @@ struct EwJob {
 };
 
 // One GPU's row block [lo, hi) of an elementwise fold.
+//
+// Chunk k uses slot k % kPipeSlots.  Three streams keep both copy engines
+// and the SMs busy at once:
+//   copy-in  : waits until compute(k - S) has consumed the slot, then H2D;
+//   compute  : waits for copy-in(k) and for copy-out(k - S) to have drained
+//              the slot's output, then the fold kernel;
+//   copy-out : waits for compute(k), then D2H.
+// Pinned caller buffers are copied directly; pageable ones go through the
+// slot's pinned staging buffers, which the host fills and empties around
+// the same events.
 int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_out) {
   std::lock_guard<std::mutex> g(d.mu);
   CK(cudaSetDevice(d.id));
-  cudaStream_t s0 = d.s[0], s1 = d.s[1];
-  CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), s0));
-  CK(cudaMemcpyAsync(d.d0, j.l, j.ies, cudaMemcpyHostToDevice, s0));
-  if (j.binary) CK(cudaMemcpyAsync((char*)d.d0 + 16, j.r, j.ies, cudaMemcpyHostToDevice, s0));
-  CK(cudaEventRecord(d.start, s0));
-  CK(cudaStreamWaitEvent(s1, d.start, 0));
+  constexpr int S = kPipeSlots;
+  CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), d.scomp));
+  CK(cudaMemcpyAsync(d.d0, j.l, j.ies, cudaMemcpyHostToDevice, d.scomp));
+  if (j.binary) CK(cudaMemcpyAsync((char*)d.d0 + 16, j.r, j.ies, cudaMemcpyHostToDevice, d.scomp));
 
   const bool lp = j.lsplat || is_pinned(j.l);
   const bool rp = !j.binary || j.rsplat || is_pinned(j.r);
   const bool op = is_pinned(j.out);
-  const bool staged = !(lp && rp && op);
   const size_t es = std::max(j.ies, j.oes);
-  uint64_t chunk = (kChunkBytes / es) / kAlignElems * kAlignElems;
-  size_t pend_off[2] = {0, 0}, pend_n[2] = {0, 0};
-  bool used[2] = {false, false};
-  int k = 0;
-  for (uint64_t off = lo; off < hi; off += chunk) {
+  const uint64_t chunk = std::max<uint64_t>(kAlignElems, (kPipeChunk / es) / kAlignElems * kAlignElems);
+  uint64_t pend_off[S] = {0}, pend_n[S] = {0};  // pageable output waiting in slot staging
+  bool used[S] = {false};
+  uint64_t k = 0;
+  for (uint64_t off = lo; off < hi; off += chunk, k++) {
+    const int t = (int)(k % S);
     const uint64_t cnt = std::min<uint64_t>(chunk, hi - off);
-    cudaStream_t s = d.s[k];
-    if (staged && used[k]) {
-      int rc = wait_event(d.ev[k]);
-      if (rc) return rc;
-      if (pend_n[k]) {
-        memcpy((char*)j.out + pend_off[k] * j.oes, d.h[k][2], pend_n[k] * j.oes);
-        pend_n[k] = 0;
+    if (used[t]) {
+      // The slot's previous chunk: its inputs are consumed once its kernel
+      // ran; its pageable output is copied out once its D2H finished.
+      CK(cudaStreamWaitEvent(d.sin, d.evcomp[t], 0));
+      if (!lp || !rp) {
+        int rc = wait_event(d.evin[t]);
+        if (rc) return rc;
+      }
+      if (pend_n[t]) {
+        int rc = wait_event(d.evout[t]);
+        if (rc) return rc;
+        memcpy((char*)j.out + pend_off[t] * j.oes, d.ph[t][2], pend_n[t] * j.oes);
+        pend_n[t] = 0;
       }
     }
     const void* ldev = d.d0;
@@ -342,21 +389,24 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
     if (!j.lsplat) {
       const void* src = (const char*)j.l + off * j.ies;
       if (!lp) {
-        memcpy(d.h[k][0], src, cnt * j.ies);
-        src = d.h[k][0];
+        memcpy(d.ph[t][0], src, cnt * j.ies);
+        src = d.ph[t][0];
       }
-      CK(cudaMemcpyAsync(d.d[k][0], src, cnt * j.ies, cudaMemcpyHostToDevice, s));
-      ldev = d.d[k][0];
+      CK(cudaMemcpyAsync(d.pd[t][0], src, cnt * j.ies, cudaMemcpyHostToDevice, d.sin));
+      ldev = d.pd[t][0];
     }
     if (j.binary && !j.rsplat) {
       const void* src = (const char*)j.r + off * j.ies;
       if (!rp) {
-        memcpy(d.h[k][1], src, cnt * j.ies);
-        src = d.h[k][1];
+        memcpy(d.ph[t][1], src, cnt * j.ies);
+        src = d.ph[t][1];
       }
-      CK(cudaMemcpyAsync(d.d[k][1], src, cnt * j.ies, cudaMemcpyHostToDevice, s));
-      rdev = d.d[k][1];
+      CK(cudaMemcpyAsync(d.pd[t][1], src, cnt * j.ies, cudaMemcpyHostToDevice, d.sin));
+      rdev = d.pd[t][1];
     }
+    CK(cudaEventRecord(d.evin[t], d.sin));
+    CK(cudaStreamWaitEvent(d.scomp, d.evin[t], 0));
+    if (used[t]) CK(cudaStreamWaitEvent(d.scomp, d.evout[t], 0));
     EwLaunch a;
     a.op = j.op;
     a.dtype = j.dtype;
@@ -364,7 +414,7 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
     a.flags = j.flags;
     a.l = ldev;
     a.r = j.binary ? rdev : nullptr;
-    a.o = d.d[k][2];
+    a.o = d.pd[t][2];
     a.n = cnt;
     a.l0 = d.d0;
     a.r0 = (char*)d.d0 + 16;
@@ -372,34 +422,35 @@ int run_block(Dev& d, const EwJob& j, uint64_t lo, uint64_t hi, dcf_status* st_o
     a.rsplat = j.rsplat;
     a.base = off;
     a.st = d.st;
-    a.stream = s;
+    a.stream = d.scomp;
     int rc = launch_ew(a);
     if (rc == DCF_EUNSUPPORTED)
       return set_err(rc, "op %d on dtype %d -> %d is not supported", j.op, j.dtype, j.out_dtype);
     if (rc) return set_err(rc, "kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    CK(cudaEventRecord(d.evcomp[t], d.scomp));
+    CK(cudaStreamWaitEvent(d.sout, d.evcomp[t], 0));
     if (op) {
-      CK(cudaMemcpyAsync((char*)j.out + off * j.oes, d.d[k][2], cnt * j.oes, cudaMemcpyDeviceToHost, s));
+      CK(cudaMemcpyAsync((char*)j.out + off * j.oes, d.pd[t][2], cnt * j.oes, cudaMemcpyDeviceToHost, d.sout));
     } else {
-      CK(cudaMemcpyAsync(d.h[k][2], d.d[k][2], cnt * j.oes, cudaMemcpyDeviceToHost, s));
-      pend_off[k] = off;
-      pend_n[k] = cnt;
+      CK(cudaMemcpyAsync(d.ph[t][2], d.pd[t][2], cnt * j.oes, cudaMemcpyDeviceToHost, d.sout));
+      pend_off[t] = off;
+      pend_n[t] = cnt;
     }
-    CK(cudaEventRecord(d.ev[k], s));
-    used[k] = true;
-    k ^= 1;
+    CK(cudaEventRecord(d.evout[t], d.sout));
+    used[t] = true;
   }
-  for (int t = 0; t < 2; t++) {
+  for (int t = 0; t < S; t++) {
     if (!used[t]) continue;
-    int rc = wait_event(d.ev[t]);
+    int rc = wait_event(d.evout[t]);
     if (rc) return rc;
     if (pend_n[t]) {
-      memcpy((char*)j.out + pend_off[t] * j.oes, d.h[t][2], pend_n[t] * j.oes);
+      memcpy((char*)j.out + pend_off[t] * j.oes, d.ph[t][2], pend_n[t] * j.oes);
       pend_n[t] = 0;
     }
   }
-  CK(cudaEventRecord(d.start, s1));
-  CK(cudaStreamWaitEvent(s0, d.start, 0));
-  return read_status(d, s0, st_out);
+  CK(cudaEventRecord(d.start, d.scomp));
+  CK(cudaStreamWaitEvent(d.s[0], d.start, 0));
+  return read_status(d, d.s[0], st_out);
 }
 
 int run_elementwise(const EwJob& j, uint64_t n, dcf_result* res) {
