@@ -301,6 +301,17 @@ int dcf_reciprocal_async(dcf_dtype dtype, const void* in, int in_splat,
 int dcf_transpose2d_async(size_t elem_size, uint64_t rows, uint64_t cols,
                           const void* in, void* out, void* stream);
 
+/* N-D permutation (as dcf_transpose) on device pointers; rank <= 8. */
+int dcf_permute_async(size_t elem_size, int rank, const int64_t* in_shape,
+                      const int64_t* perms, const void* in, void* out,
+                      void* stream);
+
+/* Splat test on device memory: afterwards status->splat_word != 0 when all
+ * n elements equal element 0 (the all-values test of Tf::splat,
+ * src/patterns/tosa/canonicalize.rs:97-100).  Reset the status first. */
+int dcf_splat_check_async(const void* in, size_t elem_size, uint64_t n,
+                          dcf_status* status, void* stream);
+
 int dcf_hex_encode_async(const void* in, uint64_t nbytes, char* out,
                          void* stream);
 int dcf_hex_decode_async(const char* in, uint64_t nchars, void* out,

@@ -1,0 +1,52 @@
+/*
+ * dcfold_opt.h — C ABI of libdcfold_opt.so, the pass driver that runs the
+ * dense-constant folds of mlirpass's pipelines on MLIR text with libdcfold.
+ *
+ * It stands in for the parts of mlirpass around the fold hooks that a
+ * fold-only run needs: reading and printing the generic form, the greedy
+ * rewrite driver (src/rewrite.rs:785-906), `canonicalize` as a bare flag
+ * (src/pass.rs:693-695) and nested `func.func(...)` pipelines whose
+ * functions the reference runs as parallel tasks (src/pass.rs:280-341), plus
+ * the `tosa-layerwise-constant-fold` pass that the reference lacks.  Only
+ * folds run: the reference's canonicalization rewrite patterns are not
+ * restated.
+ */
+#ifndef DCFOLD_OPT_H
+#define DCFOLD_OPT_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Phase timings and counters of one run (milliseconds / counts). */
+typedef struct dcf_opt_stats {
+  double parse_ms;   /* text -> IR */
+  double run_ms;     /* the pipeline, including host<->device transfers and
+                        bringing every folded constant back to host memory */
+  double print_ms;   /* IR -> text */
+  unsigned long long folds, refused, h2d_bytes, d2h_bytes, batches;
+} dcf_opt_stats;
+
+/* Run `pipeline` ("canonicalize", or "builtin.module(func.func(P,...))" with
+ * P in canonicalize, tosa-layerwise-constant-fold) over the module `text`
+ * on GPUs 0..n_gpus-1 (n_gpus < 0: every GPU).  n_gpus == 0 runs host-only:
+ * parsing, printing and the folds decided without element work (shortcuts)
+ * succeed, and any fold that needs element work fails with an error; there
+ * is no CPU fallback.  Chunks separated by "// -----" are run separately
+ * when split_input_file is nonzero.  On success *out is a malloc'ed
+ * printed module (free with dcf_opt_free) and the return value is 0;
+ * otherwise a negative code and dcf_opt_last_error() says why. */
+int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int split_input_file,
+                char** out, size_t* out_len, dcf_opt_stats* stats);
+
+void dcf_opt_free(char* p);
+
+const char* dcf_opt_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -103,6 +103,9 @@ SIGNATURES = {
     "dcf_convert_async": (_I, [_I, _I, _I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
     "dcf_reciprocal_async": (_I, [_I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
     "dcf_transpose2d_async": (_I, [_SZ, _U64, _U64, _VP, _VP, _VP]),
+    "dcf_permute_async": (_I, [_SZ, _I, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _VP, _VP,
+                               _VP]),
+    "dcf_splat_check_async": (_I, [_VP, _SZ, _U64, _VP, _VP]),
     "dcf_hex_encode_async": (_I, [_VP, _U64, _VP, _VP]),
     "dcf_hex_decode_async": (_I, [_VP, _U64, _VP, _VP, _VP]),
     "dcf_status_read": (_I, [_VP, _VP, _RP]),

@@ -83,6 +83,37 @@ def build_lib(verbose: bool = False, force: bool = False) -> str:
     return LIB
 
 
+OPT_SOURCES = ["ir.cpp", "engine.cpp", "fold.cpp", "main.cpp"]
+OPT_LIB = os.path.join(PKG, "libdcfold_opt.so")
+OPT_BIN = os.path.join(PKG, "dcfold-opt")
+
+
+def _cuda_home() -> str:
+    return os.path.dirname(os.path.dirname(os.path.realpath(nvcc())))
+
+
+def build_opt(force: bool = False) -> list[str]:
+    """The pass driver: libdcfold_opt.so and the dcfold-opt executable."""
+    srcs = [os.path.join(PKG, "opt", f) for f in OPT_SOURCES]
+    deps = srcs + [os.path.join(PKG, "opt", f) for f in ("ir.h", "engine.h", "fold.h")] + \
+        [os.path.join(ROOT, "include", "dcfold.h"), os.path.join(ROOT, "include", "dcfold_opt.h"), LIB]
+    cuda = _cuda_home()
+    cxx = os.environ.get("CXX", "g++")
+    common = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-I", os.path.join(cuda, "include")]
+    link = ["-L", PKG, "-ldcfold", "-Wl,-rpath,$ORIGIN", "-L", os.path.join(cuda, "lib64"),
+            "-lcudart_static", "-lpthread", "-ldl", "-lrt"]
+    out = []
+    for target, extra in ((OPT_LIB, ["-shared"]), (OPT_BIN, ["-DDCFOLD_OPT_MAIN"])):
+        if force or _stale(target, deps):
+            cmd = [cxx, *common, *extra, "-o", target, *srcs, *link]
+            res = subprocess.run(cmd, capture_output=True, text=True)
+            if res.returncode:
+                sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+                raise RuntimeError(f"build of {os.path.basename(target)} failed")
+        out.append(target)
+    return out
+
+
 def build_oracle(force: bool = False) -> str:
     os.makedirs(os.path.dirname(ORACLE_LIB), exist_ok=True)
     deps = [ORACLE_SRC, os.path.join(ROOT, "oracle", "dcf_oracle.h"), os.path.join(ROOT, "include", "dcfold.h")]
@@ -101,6 +132,8 @@ def main(argv: list[str]) -> None:
     force = "--force" in argv
     if "--oracle" not in argv:
         print(build_lib(verbose="-v" in argv, force=force))
+        for t in build_opt(force=force):
+            print(t)
     if "--lib" not in argv:
         print(build_oracle(force=force))
 

@@ -996,6 +996,39 @@ int dcf_transpose2d_async(size_t elem_size, uint64_t rows, uint64_t cols, const 
   return DCF_OK;
 }
 
+int dcf_permute_async(size_t elem_size, int rank, const int64_t* in_shape, const int64_t* perms, const void* in,
+                      void* out, void* stream) {
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
+    return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
+  if (rank < 1 || rank > 8 || !in_shape || !perms) return set_err(DCF_EINVAL, "bad rank or shape");
+  uint64_t total = 1;
+  bool seen[8] = {false};
+  for (int i = 0; i < rank; i++) {
+    if (in_shape[i] < 0) return set_err(DCF_EINVAL, "negative dim");
+    if (perms[i] < 0 || perms[i] >= rank || seen[perms[i]]) return set_err(DCF_EINVAL, "perms is not a permutation");
+    seen[perms[i]] = true;
+    total *= (uint64_t)in_shape[i];
+  }
+  if (total == 0) return DCF_OK;
+  int rc = select_device(out);
+  if (rc) return rc;
+  rc = launch_permute(elem_size, rank, in_shape, perms, in, out, (cudaStream_t)stream);
+  if (rc) return set_err(rc, "permute launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return DCF_OK;
+}
+
+int dcf_splat_check_async(const void* in, size_t elem_size, uint64_t n, dcf_status* status, void* stream) {
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
+    return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
+  if (!status) return set_err(DCF_EINVAL, "null status");
+  if (n <= 1) return DCF_OK;
+  int rc = select_device(status);
+  if (rc) return rc;
+  rc = launch_splat_check(in, elem_size, n, status, (cudaStream_t)stream);
+  if (rc) return set_err(rc, "splat launch failed");
+  return DCF_OK;
+}
+
 int dcf_hex_encode_async(const void* in, uint64_t nbytes, char* out, void* stream) {
   if (nbytes == 0) return DCF_OK;
   int rc = select_device(out);

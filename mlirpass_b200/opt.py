@@ -1,0 +1,67 @@
+"""Binding of libdcfold_opt.so: run mlirpass pipelines' dense-constant folds
+on MLIR text (include/dcfold_opt.h).
+
+    out, stats = run(text, "canonicalize")
+    out, stats = run(text, "builtin.module(func.func(tosa-layerwise-constant-fold,canonicalize))", n_gpus=8)
+
+n_gpus=0 runs host-only: parsing, printing and the folds decided without
+element work succeed; a fold that needs element work raises (no CPU
+fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdcfold_opt.so")
+BIN_PATH = os.path.join(_HERE, "dcfold-opt")
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("parse_ms", ctypes.c_double), ("run_ms", ctypes.c_double), ("print_ms", ctypes.c_double),
+                ("folds", ctypes.c_ulonglong), ("refused", ctypes.c_ulonglong), ("h2d_bytes", ctypes.c_ulonglong),
+                ("d2h_bytes", ctypes.c_ulonglong), ("batches", ctypes.c_ulonglong)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+class OptError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m mlirpass_b200.build` first")
+        L = ctypes.CDLL(LIB_PATH)
+        L.dcf_opt_run.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+                                  ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t),
+                                  ctypes.POINTER(Stats)]
+        L.dcf_opt_run.restype = ctypes.c_int
+        L.dcf_opt_free.argtypes = [ctypes.c_void_p]
+        L.dcf_opt_last_error.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def run(text: str | bytes, pipeline: str, n_gpus: int = 1, split_input_file: bool = False):
+    """Run `pipeline` over `text`; returns (printed module, stats dict)."""
+    data = text.encode() if isinstance(text, str) else text
+    out = ctypes.c_void_p()
+    n = ctypes.c_size_t()
+    st = Stats()
+    rc = lib().dcf_opt_run(data, len(data), pipeline.encode(), n_gpus, int(split_input_file), ctypes.byref(out),
+                           ctypes.byref(n), ctypes.byref(st))
+    if rc != 0:
+        raise OptError(lib().dcf_opt_last_error().decode())
+    try:
+        s = ctypes.string_at(out, n.value).decode()
+    finally:
+        lib().dcf_opt_free(out)
+    return s, st.as_dict()

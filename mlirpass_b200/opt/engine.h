@@ -1,0 +1,93 @@
+// engine.h — the device side of dcfold-opt: constant residency on a GPU and
+// execution of element-level fold requests through libdcfold's C ABI.
+//
+// Constants live where they are cheapest to use next.  A constant parsed
+// from `dense<"0x…">` text is uploaded as text on first use and decoded on
+// the device (dcf_hex_decode_async); a fold result stays on the device
+// until the printer (or a host-side shortcut) needs it, so a chain of folds
+// never round-trips through the host.  Results that come out all-equal are
+// kept as one host-side element, as MLIR stores a splat.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/dcfold.h"
+#include "ir.h"
+
+namespace dco {
+
+class DeviceBuf {
+ public:
+  DeviceBuf(int device, size_t bytes);
+  ~DeviceBuf();
+  DeviceBuf(const DeviceBuf&) = delete;
+  DeviceBuf& operator=(const DeviceBuf&) = delete;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int device = 0;
+};
+
+// One element-level fold.  The greedy driver fills the inputs; the engine
+// fills the outcome.
+struct FoldRequest {
+  enum Kind { BINARY, CONVERT, RECIPROCAL, PERMUTE, SPLAT_SCAN } kind = BINARY;
+  int op = 0, dtype = 0, out_dtype = 0;
+  uint32_t flags = 0;
+  DenseP lhs, rhs;
+  uint64_t n = 0;                       // result elements
+  std::vector<int64_t> shape, perms;    // PERMUTE
+  TypeP out_ty;                         // attribute type of the result
+  bool out_elements = true;
+  // outcome
+  bool folded = false;
+  uint64_t first_fail = ~0ull;
+  DenseP out;
+};
+
+struct EngineStats {
+  uint64_t h2d_bytes = 0, d2h_bytes = 0, requests = 0, batches = 0;
+  double device_ms = 0;  // sum of batch wall times
+};
+
+// device < 0 makes a host-only engine: parsing, printing and the folds that
+// the host decides alone (shortcuts) work, and any element work throws.
+class Engine {
+ public:
+  explicit Engine(int device);
+  ~Engine();
+  int device() const { return dev_; }
+
+  // Run every request (all belong to this engine's device).  Throws on a
+  // runtime error; a refused fold is an outcome, not an error.
+  void execute(const std::vector<FoldRequest*>& reqs);
+
+  // Make a constant resident on this device.
+  void to_device(DenseValue& v);
+  // Make its bytes available on the host (downloading if needed).
+  void to_host(DenseValue& v);
+  // Uppercase hex digits of all its bytes (encoded on the device when
+  // the value is there).
+  std::string hex_of(DenseValue& v);
+  uint64_t bits0_of(DenseValue& v);
+  // Whether every value equals the first (cached in v.all_equal).
+  bool all_equal(DenseValue& v);
+
+  EngineStats stats;
+
+ private:
+  int dev_;
+  cudaStream_t s_ = nullptr;
+  std::unique_ptr<DeviceBuf> status_;   // dcf_status slots of a batch
+  size_t status_cap_ = 0;
+  std::unique_ptr<DeviceBuf> aux_;      // status word of uploads and scans outside a batch
+  void set_device();
+  void check(int rc, const char* what);
+  void sync();
+  dcf_status* statuses(size_t n);
+};
+
+}  // namespace dco

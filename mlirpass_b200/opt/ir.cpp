@@ -1,0 +1,979 @@
+// ir.cpp — types, IR mutation, the generic-form parser and printer, and the
+// MLIR float / int literal codecs of dcfold-opt.
+#include "ir.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+
+#include "../../include/dcfold.h"
+
+namespace dco {
+
+// ================================================================== types
+
+static int dtype_of_elem(const std::string& e) {
+  static const std::pair<const char*, int> table[] = {
+      {"i1", DCF_I1},     {"i8", DCF_I8},       {"i16", DCF_I16},        {"i32", DCF_I32},
+      {"i64", DCF_I64},   {"index", DCF_I64},   {"f16", DCF_F16},        {"bf16", DCF_BF16},
+      {"f32", DCF_F32},   {"f64", DCF_F64},     {"f8E5M2", DCF_F8E5M2}, {"f8E4M3", DCF_F8E4M3},
+      {"f8E3M4", DCF_F8E3M4}};
+  for (auto& [n, d] : table)
+    if (e == n) return d;
+  return 0;
+}
+
+bool Type::is_float() const { return dtype >= DCF_F16 && dtype <= DCF_F8E3M4; }
+bool Type::is_int() const { return dtype >= DCF_I1 && dtype <= DCF_I64; }
+
+int64_t Type::count() const {
+  if (!shaped()) return 1;
+  int64_t n = 1;
+  for (int64_t d : shape) n *= d;
+  return n;
+}
+
+static Type make_type(const std::string& text) {
+  Type t;
+  t.text = text;
+  auto shaped = [&](const char* pre) { return text.rfind(pre, 0) == 0 && text.back() == '>'; };
+  if (shaped("tensor<") || shaped("vector<")) {
+    t.kind = text[0] == 't' ? "tensor" : "vector";
+    std::string body = text.substr(7, text.size() - 8);
+    // An encoding or other trailing parameter makes the type opaque here.
+    int depth = 0;
+    for (char c : body) {
+      if (c == '<' || c == '(' || c == '[') depth++;
+      if (c == '>' || c == ')' || c == ']') depth--;
+      if (c == ',' && depth == 0) {
+        t.kind = "other";
+        return t;
+      }
+    }
+    size_t p = 0;
+    for (;;) {
+      size_t x = body.find('x', p);
+      if (x == std::string::npos) break;
+      std::string dim = body.substr(p, x - p);
+      bool digits = !dim.empty();
+      for (char c : dim) digits = digits && (c >= '0' && c <= '9');
+      if (digits) {
+        t.shape.push_back(std::stoll(dim));
+      } else if (dim == "?" || (!dim.empty() && dim[0] == '[')) {
+        t.dynamic = true;
+        t.shape.push_back(-1);
+      } else {
+        break;
+      }
+      p = x + 1;
+    }
+    t.elem = body.substr(p);
+  } else {
+    t.kind = "";
+    t.elem = text;
+  }
+  t.dtype = dtype_of_elem(t.elem);
+  if (t.kind == "" && !t.dtype) t.kind = "other";
+  return t;
+}
+
+TypeP type_of(const std::string& text) {
+  static std::mutex mu;
+  static std::unordered_map<std::string, TypeP> interned;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = interned.find(text);
+  if (it != interned.end()) return it->second;
+  auto t = std::make_shared<const Type>(make_type(text));
+  interned.emplace(text, t);
+  return t;
+}
+
+TypeP with_element(const TypeP& t, const std::string& elem) {
+  if (!t->shaped()) return type_of(elem);
+  std::string s = t->kind + "<";
+  for (int64_t d : t->shape) s += (d < 0 ? std::string("?") : std::to_string(d)) + "x";
+  return type_of(s + elem + ">");
+}
+
+TypeP element_type(const TypeP& t) { return t->shaped() ? type_of(t->elem) : t; }
+
+uint64_t DenseValue::bits0() const {
+  uint64_t v = 0;
+  if (!host.empty()) memcpy(&v, host.data(), es);
+  return v;
+}
+
+// ================================================================ module
+
+const std::string* Op::prop(const std::string& key) const {
+  for (auto& kv : props)
+    if (kv.first == key) return &kv.second;
+  return nullptr;
+}
+
+void Op::set_prop(const std::string& key, const std::string& text) {
+  for (auto& kv : props)
+    if (kv.first == key) {
+      kv.second = text;
+      return;
+    }
+  props.emplace_back(key, text);
+}
+
+Op* Module::new_op(const std::string& name) {
+  ops_.push_back(std::make_unique<Op>());
+  ops_.back()->name = name;
+  return ops_.back().get();
+}
+
+Value* Module::new_value(TypeP ty) {
+  values_.push_back(std::make_unique<Value>());
+  values_.back()->ty = std::move(ty);
+  return values_.back().get();
+}
+
+Block* Module::new_block() {
+  blocks_.push_back(std::make_unique<Block>());
+  return blocks_.back().get();
+}
+
+Region* Module::new_region() {
+  regions_.push_back(std::make_unique<Region>());
+  return regions_.back().get();
+}
+
+void Module::insert_before(Op* op, Op* before) {
+  Block* b = before->parent;
+  op->parent = b;
+  op->pos = b->ops.insert(before->pos, op);
+}
+
+void Module::append(Op* op, Block* b) {
+  op->parent = b;
+  op->pos = b->ops.insert(b->ops.end(), op);
+}
+
+void Module::detach(Op* op) {
+  if (!op->parent) return;
+  op->parent->ops.erase(op->pos);
+  op->parent = nullptr;
+}
+
+static void drop_use(Value* v, Op* user) {
+  for (size_t i = 0; i < v->uses.size(); i++)
+    if (v->uses[i] == user) {
+      v->uses.erase(v->uses.begin() + (long)i);
+      return;
+    }
+}
+
+void Module::erase(Op* op) {
+  for (Region* r : op->regions)
+    for (Block* b : r->blocks)
+      while (!b->ops.empty()) {
+        Op* inner = b->ops.back();
+        for (Value* res : inner->results) res->uses.clear();
+        erase(inner);
+      }
+  for (Value* v : op->operands) drop_use(v, op);
+  op->operands.clear();
+  detach(op);
+  op->erased = true;
+}
+
+void Module::set_operand(Op* op, size_t i, Value* v) {
+  drop_use(op->operands[i], op);
+  op->operands[i] = v;
+  v->uses.push_back(op);
+}
+
+void Module::replace_all_uses(Value* from, Value* to) {
+  if (from == to) return;
+  std::vector<Op*> users = from->uses;
+  for (Op* u : users)
+    for (size_t i = 0; i < u->operands.size(); i++)
+      if (u->operands[i] == from) set_operand(u, i, to);
+}
+
+// ======================================================= literal codecs
+
+struct Layout {
+  int E, M;
+};
+
+static bool layout_of(int dtype, Layout* l) {
+  switch (dtype) {
+    case DCF_F16: *l = {5, 10}; return true;
+    case DCF_BF16: *l = {8, 7}; return true;
+    case DCF_F32: *l = {8, 23}; return true;
+    case DCF_F64: *l = {11, 52}; return true;
+    case DCF_F8E5M2: *l = {5, 2}; return true;
+    case DCF_F8E4M3: *l = {4, 3}; return true;
+    case DCF_F8E3M4: *l = {3, 4}; return true;
+    default: return false;
+  }
+}
+
+static int width_of(int dtype) {
+  switch (dtype) {
+    case DCF_I1: return 1;
+    case DCF_I8: return 8;
+    case DCF_I16: return 16;
+    case DCF_I32: return 32;
+    case DCF_I64: return 64;
+    default: return 0;
+  }
+}
+
+static size_t elem_bytes(int dtype) { return dcf_dtype_size((dcf_dtype)dtype); }
+
+// Nearest-even rounding of a finite double into a narrow IEEE-like layout.
+static uint64_t narrow_from_double(double x, Layout L) {
+  uint64_t d;
+  memcpy(&d, &x, 8);
+  const uint64_t sign = (d >> 63) << (L.E + L.M);
+  if (x != x) return sign | ((((1ull << L.E) - 1)) << L.M) | (1ull << (L.M - 1));
+  if (std::isinf(x)) return sign | (((1ull << L.E) - 1) << L.M);
+  if (x == 0) return sign;
+  int e2;
+  double fr = std::frexp(std::fabs(x), &e2);  // |x| = fr * 2^e2, fr in [0.5, 1)
+  uint64_t sig = (uint64_t)std::ldexp(fr, 53);  // exact: 53-bit significand
+  int exp = e2 - 53;
+  const int bias = (1 << (L.E - 1)) - 1, emin = 1 - bias;
+  const int p = 63 - __builtin_clzll(sig);
+  const int e = p + exp;
+  const int q = (e < emin) ? emin - L.M : e - L.M;
+  const int sh = q - exp;
+  uint64_t r;
+  if (sh <= 0) {
+    r = sig << (-sh);
+  } else if (sh >= 64) {
+    r = 0;
+  } else {
+    const uint64_t rem = sig & ((1ull << sh) - 1), half = 1ull << (sh - 1);
+    r = sig >> sh;
+    if (rem > half || (rem == half && (r & 1))) r++;
+  }
+  uint64_t bits = (e < emin) ? r : (((uint64_t)(e + bias - 1) << L.M) + r);
+  if ((bits >> L.M) >= ((1ull << L.E) - 1)) bits = ((1ull << L.E) - 1) << L.M;
+  return sign | bits;
+}
+
+static double widen_to_double(uint64_t b, Layout L) {
+  const bool neg = (b >> (L.E + L.M)) & 1;
+  const uint64_t ef = (b >> L.M) & ((1ull << L.E) - 1), m = b & ((1ull << L.M) - 1);
+  const int bias = (1 << (L.E - 1)) - 1;
+  double v;
+  if (ef == ((1ull << L.E) - 1)) v = m ? NAN : INFINITY;
+  else if (ef == 0) v = std::ldexp((double)m, 1 - bias - L.M);
+  else v = std::ldexp((double)(m | (1ull << L.M)), (int)ef - bias - L.M);
+  return neg ? -v : v;
+}
+
+bool parse_float_literal(const std::string& tok, int dtype, uint64_t* bits) {
+  Layout L;
+  if (!layout_of(dtype, &L)) return false;
+  if (tok.size() > 2 && tok[0] == '0' && (tok[1] == 'x' || tok[1] == 'X')) {
+    *bits = strtoull(tok.c_str(), nullptr, 16);
+    return true;
+  }
+  char* end = nullptr;
+  if (dtype == DCF_F32) {
+    float f = strtof(tok.c_str(), &end);
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    *bits = u;
+  } else {
+    double x = strtod(tok.c_str(), &end);
+    if (dtype == DCF_F64) memcpy(bits, &x, 8);
+    else *bits = narrow_from_double(x, L);
+  }
+  return end && *end == 0;
+}
+
+// MLIR prints a float in "%.6e" form when that form parses back to the same
+// bits, and otherwise in a form that keeps every bit; the hex bit pattern
+// (which MLIR also accepts) stands in for that second form here.
+std::string print_float_literal(uint64_t bits, int dtype) {
+  Layout L;
+  if (!layout_of(dtype, &L)) return "0";
+  const double v = (dtype == DCF_F64) ? [&] { double d; memcpy(&d, &bits, 8); return d; }()
+                                       : widen_to_double(bits, L);
+  if (std::isfinite(v)) {
+    char buf[64];
+    snprintf(buf, sizeof buf, "%.6e", v);
+    uint64_t back = 0;
+    if (parse_float_literal(buf, dtype, &back) && back == bits) return buf;
+  }
+  char buf[40];
+  snprintf(buf, sizeof buf, "0x%0*llX", (int)(2 * elem_bytes(dtype)), (unsigned long long)bits);
+  return buf;
+}
+
+std::string print_int_literal(uint64_t bits, int dtype) {
+  const int w = width_of(dtype);
+  if (w == 1) return (bits & 1) ? "true" : "false";
+  if (w < 64) {
+    const uint64_t m = 1ull << (w - 1);
+    bits &= (1ull << w) - 1;
+    return std::to_string((long long)((bits ^ m) - m));
+  }
+  return std::to_string((long long)bits);
+}
+
+static bool parse_int_literal(const std::string& tok, int dtype, uint64_t* bits) {
+  const int w = width_of(dtype);
+  if (!w) return false;
+  if (tok == "true") {
+    *bits = 1;
+    return true;
+  }
+  if (tok == "false") {
+    *bits = 0;
+    return true;
+  }
+  char* end = nullptr;
+  uint64_t v;
+  if (!tok.empty() && tok[0] == '-') v = (uint64_t)strtoll(tok.c_str(), &end, 0);
+  else v = strtoull(tok.c_str(), &end, 0);
+  if (!end || *end) return false;
+  *bits = (w == 64) ? v : (v & ((1ull << w) - 1));
+  return true;
+}
+
+// =================================================================== parse
+
+namespace {
+
+[[noreturn]] void fail(const std::string& msg, size_t at) {
+  throw std::runtime_error("parse error at offset " + std::to_string(at) + ": " + msg);
+}
+
+std::string trim(const std::string& s) {
+  size_t a = 0, b = s.size();
+  while (a < b && isspace((unsigned char)s[a])) a++;
+  while (b > a && isspace((unsigned char)s[b - 1])) b--;
+  return s.substr(a, b - a);
+}
+
+// Split at top-level occurrences of `sep`, honouring (), [], {}, <> nesting,
+// string literals and the "->" arrow.
+std::vector<std::string> split_top(const std::string& s, char sep) {
+  std::vector<std::string> out;
+  int depth = 0;
+  size_t start = 0;
+  bool str = false;
+  for (size_t i = 0; i < s.size(); i++) {
+    const char c = s[i];
+    if (str) {
+      if (c == '\\') i++;
+      else if (c == '"') str = false;
+      continue;
+    }
+    if (c == '"') str = true;
+    else if (c == '-' && i + 1 < s.size() && s[i + 1] == '>') i++;
+    else if (c == '(' || c == '[' || c == '{' || c == '<') depth++;
+    else if (c == ')' || c == ']' || c == '}' || c == '>') depth--;
+    else if (c == sep && depth == 0) {
+      out.push_back(trim(s.substr(start, i - start)));
+      start = i + 1;
+    }
+  }
+  std::string last = trim(s.substr(start));
+  if (!last.empty() || !out.empty()) out.push_back(last);
+  return out;
+}
+
+void flatten_list(const std::string& s, std::vector<std::string>& out) {
+  std::string t = trim(s);
+  if (!t.empty() && t[0] == '[') {
+    for (auto& part : split_top(t.substr(1, t.size() - 2), ',')) flatten_list(part, out);
+  } else if (!t.empty()) {
+    out.push_back(t);
+  }
+}
+
+class Parser {
+ public:
+  Parser(const std::string& s, Module& m) : s_(s), m_(m) {}
+
+  Op* parse_top() {
+    scopes_.emplace_back();
+    ws();
+    Op* op = parse_op(nullptr);
+    ws();
+    if (p_ != s_.size()) fail("trailing text", p_);
+    close_scope();
+    return op;
+  }
+
+ private:
+  const std::string& s_;
+  Module& m_;
+  size_t p_ = 0;
+  struct Scope {
+    std::unordered_map<std::string, std::vector<Value*>> names;
+    std::unordered_map<std::string, Value*> forward;
+  };
+  std::vector<Scope> scopes_;
+
+  void ws() {
+    for (;;) {
+      while (p_ < s_.size() && isspace((unsigned char)s_[p_])) p_++;
+      if (p_ + 1 < s_.size() && s_[p_] == '/' && s_[p_ + 1] == '/') {
+        while (p_ < s_.size() && s_[p_] != '\n') p_++;
+        continue;
+      }
+      break;
+    }
+  }
+  bool peek(char c) {
+    ws();
+    return p_ < s_.size() && s_[p_] == c;
+  }
+  bool peek(const char* t) {
+    ws();
+    return s_.compare(p_, strlen(t), t) == 0;
+  }
+  bool eat(char c) {
+    if (!peek(c)) return false;
+    p_++;
+    return true;
+  }
+  bool eat(const char* t) {
+    if (!peek(t)) return false;
+    p_ += strlen(t);
+    return true;
+  }
+  void expect(char c) {
+    if (!eat(c)) fail(std::string("expected '") + c + "'", p_);
+  }
+
+  // A balanced span starting here, ending before a top-level char in `stops`.
+  std::string span(const char* stops) {
+    ws();
+    const size_t start = p_;
+    int depth = 0;
+    bool str = false;
+    for (; p_ < s_.size(); p_++) {
+      const char c = s_[p_];
+      if (str) {
+        if (c == '\\') p_++;
+        else if (c == '"') str = false;
+        continue;
+      }
+      if (depth == 0 && strchr(stops, c)) break;
+      if (c == '"') str = true;
+      else if (c == '-' && p_ + 1 < s_.size() && s_[p_ + 1] == '>') p_++;
+      else if (c == '(' || c == '[' || c == '{' || c == '<') depth++;
+      else if (c == ')' || c == ']' || c == '}' || c == '>') {
+        if (depth == 0) break;
+        depth--;
+      }
+    }
+    return trim(s_.substr(start, p_ - start));
+  }
+
+  std::string ident() {
+    ws();
+    const size_t start = p_;
+    while (p_ < s_.size() && (isalnum((unsigned char)s_[p_]) || strchr("_$.-#%^", s_[p_]))) p_++;
+    return s_.substr(start, p_ - start);
+  }
+
+  void close_scope() {
+    Scope& sc = scopes_.back();
+    if (!sc.forward.empty()) fail("use of undefined value " + sc.forward.begin()->first, p_);
+    scopes_.pop_back();
+  }
+
+  Value* lookup(const std::string& ref, TypeP ty) {
+    std::string name = ref;
+    size_t idx = 0;
+    const size_t hash = ref.find('#');
+    if (hash != std::string::npos) {
+      name = ref.substr(0, hash);
+      idx = std::stoul(ref.substr(hash + 1));
+    }
+    for (auto it = scopes_.rbegin(); it != scopes_.rend(); ++it) {
+      auto f = it->names.find(name);
+      if (f != it->names.end()) {
+        if (idx >= f->second.size()) fail("result index out of range in " + ref, p_);
+        return f->second[idx];
+      }
+    }
+    Scope& sc = scopes_.back();
+    auto f = sc.forward.find(ref);
+    if (f != sc.forward.end()) return f->second;
+    Value* v = m_.new_value(std::move(ty));
+    sc.forward.emplace(ref, v);
+    return v;
+  }
+
+  void define(const std::string& name, const std::vector<Value*>& vals) {
+    Scope& sc = scopes_.back();
+    for (size_t i = 0; i < vals.size(); i++) {
+      const std::string ref = vals.size() == 1 ? name : name + "#" + std::to_string(i);
+      for (const std::string& key : {ref, name + "#" + std::to_string(i)}) {
+        auto f = sc.forward.find(key);
+        if (f != sc.forward.end()) {
+          m_.replace_all_uses(f->second, vals[i]);
+          sc.forward.erase(f);
+        }
+      }
+    }
+    sc.names[name] = vals;
+  }
+
+  static std::vector<std::string> type_list(const std::string& t) {
+    std::string s = trim(t);
+    if (!s.empty() && s[0] == '(' && s.back() == ')') {
+      // a parenthesised list, unless it is a function type "(..) -> .."
+      int depth = 0;
+      size_t close = 0;
+      for (size_t i = 0; i < s.size(); i++) {
+        if (s[i] == '(') depth++;
+        if (s[i] == ')' && --depth == 0) {
+          close = i;
+          break;
+        }
+      }
+      if (close == s.size() - 1) {
+        std::string inner = s.substr(1, s.size() - 2);
+        if (trim(inner).empty()) return {};
+        return split_top(inner, ',');
+      }
+    }
+    return {s};
+  }
+
+  Block* parse_block_label(Region* r) {
+    Block* b = m_.new_block();
+    b->parent = r;
+    b->label = ident();
+    if (eat('(')) {
+      if (!eat(')')) {
+        for (;;) {
+          std::string name = ident();
+          expect(':');
+          std::string ty = span(",)");
+          Value* v = m_.new_value(type_of(ty));
+          v->owner = b;
+          v->index = (int)b->args.size();
+          v->name = name;
+          b->args.push_back(v);
+          define(name, {v});
+          if (eat(')')) break;
+          expect(',');
+        }
+      }
+    }
+    expect(':');
+    return b;
+  }
+
+  Region* parse_region(Op* parent) {
+    Region* r = m_.new_region();
+    r->parent = parent;
+    expect('{');
+    Block* cur = nullptr;
+    while (!peek('}')) {
+      if (peek('^')) {
+        cur = parse_block_label(r);
+        r->blocks.push_back(cur);
+        continue;
+      }
+      if (!cur) {
+        cur = m_.new_block();
+        cur->parent = r;
+        r->blocks.push_back(cur);
+      }
+      parse_op(cur);
+    }
+    expect('}');
+    return r;
+  }
+
+  Op* parse_op(Block* blk) {
+    std::vector<std::pair<std::string, int>> res;  // name, count
+    ws();
+    if (peek('%')) {
+      for (;;) {
+        std::string name = ident();
+        int count = 1;
+        if (eat(':')) count = std::stoi(ident());
+        res.emplace_back(name, count);
+        if (!eat(',')) break;
+      }
+      expect('=');
+    }
+    ws();
+    if (!eat('"')) fail("expected an op name string", p_);
+    const size_t q = s_.find('"', p_);
+    if (q == std::string::npos) fail("unterminated op name", p_);
+    Op* op = m_.new_op(s_.substr(p_, q - p_));
+    p_ = q + 1;
+    expect('(');
+    std::vector<std::string> operand_refs;
+    if (!eat(')')) {
+      std::string list = span(")");
+      expect(')');
+      operand_refs = split_top(list, ',');
+    }
+    if (peek('[')) {
+      const size_t a = p_;
+      p_++;
+      span("]");
+      expect(']');
+      op->successors = s_.substr(a, p_ - a);
+    }
+    if (eat("<{")) {
+      std::string body = span("}");
+      expect('}');
+      expect('>');
+      for (auto& entry : split_top(body, ',')) {
+        const size_t eq = entry.find('=');
+        if (eq == std::string::npos) op->props.emplace_back(trim(entry), "");
+        else op->props.emplace_back(trim(entry.substr(0, eq)), trim(entry.substr(eq + 1)));
+      }
+    }
+    const bool isolated = op->name == "func.func" || op->name == "builtin.module";
+    if (peek("({")) {
+      expect('(');
+      for (;;) {
+        if (isolated) scopes_.emplace_back();
+        op->regions.push_back(parse_region(op));
+        if (isolated) close_scope();
+        if (eat(')')) break;
+        expect(',');
+      }
+    }
+    if (peek('{')) {
+      const size_t a = p_;
+      p_++;
+      span("}");
+      expect('}');
+      op->attrs = s_.substr(a, p_ - a);
+    }
+    expect(':');
+    std::string fnty = span("\n");
+    // trailing location
+    const size_t locp = fnty.rfind(" loc(");
+    if (locp != std::string::npos) {
+      op->loc = fnty.substr(locp + 1);
+      fnty = trim(fnty.substr(0, locp));
+    }
+    const size_t arrow = [&] {
+      int depth = 0;
+      for (size_t i = 0; i + 1 < fnty.size(); i++) {
+        const char c = fnty[i];
+        if (c == '(' || c == '<' || c == '[' || c == '{') depth++;
+        if (c == ')' || c == '>' || c == ']' || c == '}') depth--;
+        if (c == '-' && fnty[i + 1] == '>' && depth == 0) return i;
+      }
+      return std::string::npos;
+    }();
+    if (arrow == std::string::npos) fail("expected a function type", p_);
+    const std::vector<std::string> in_types = type_list(fnty.substr(0, arrow));
+    const std::vector<std::string> out_types = type_list(fnty.substr(arrow + 2));
+    if (in_types.size() != operand_refs.size()) fail("operand count does not match the function type", p_);
+    for (size_t i = 0; i < operand_refs.size(); i++) {
+      Value* v = lookup(operand_refs[i], type_of(in_types[i]));
+      op->operands.push_back(v);
+      v->uses.push_back(op);
+    }
+    size_t total = 0;
+    for (auto& r : res) total += (size_t)r.second;
+    if (total != out_types.size()) fail("result count does not match the function type", p_);
+    size_t k = 0;
+    for (auto& r : res) {
+      std::vector<Value*> vals;
+      for (int i = 0; i < r.second; i++, k++) {
+        Value* v = m_.new_value(type_of(out_types[k]));
+        v->def = op;
+        v->index = (int)k;
+        op->results.push_back(v);
+        vals.push_back(v);
+      }
+      define(r.first, vals);
+    }
+    if (res.empty())
+      for (size_t i = 0; i < out_types.size(); i++) {
+        Value* v = m_.new_value(type_of(out_types[i]));
+        v->def = op;
+        v->index = (int)i;
+        op->results.push_back(v);
+      }
+    if (blk) m_.append(op, blk);
+    attach_constant(op);
+    return op;
+  }
+
+  // Decode the value of a constant-like op into a DenseValue.
+  void attach_constant(Op* op) {
+    if (op->name == "ub.poison") {
+      if (op->results.size() == 1) {
+        auto d = std::make_shared<DenseValue>();
+        d->ty = op->results[0]->ty;
+        d->poison = true;
+        op->cst = d;
+      }
+      return;
+    }
+    const char* key = op->name == "arith.constant" ? "value" : op->name == "tosa.const" ? "values" : nullptr;
+    if (!key || op->results.size() != 1) return;
+    const std::string* text = op->prop(key);
+    if (!text) return;
+    std::string lit = *text, ty_text;
+    // split "literal : type" at the last top-level " : "
+    {
+      auto parts = split_top(lit, ':');
+      if (parts.size() >= 2) {
+        ty_text = parts.back();
+        lit = lit.substr(0, lit.rfind(':'));
+        lit = trim(lit);
+      }
+    }
+    TypeP ty = ty_text.empty() ? (lit == "true" || lit == "false" ? type_of("i1") : op->results[0]->ty)
+                               : type_of(ty_text);
+    if (!ty->dtype) return;
+    auto d = std::make_shared<DenseValue>();
+    d->ty = ty;
+    d->dtype = ty->dtype;
+    d->es = elem_bytes(ty->dtype);
+    const bool is_float = ty->is_float();
+    auto encode = [&](const std::string& tok, uint64_t* bits) {
+      return is_float ? parse_float_literal(tok, ty->dtype, bits) : parse_int_literal(tok, ty->dtype, bits);
+    };
+    if (lit.rfind("dense<", 0) == 0) {
+      if (!ty->static_shape()) return;
+      d->elements = true;
+      std::string body = trim(lit.substr(6, lit.size() - 7));
+      if (body.size() > 3 && body[0] == '"' && body[1] == '0' && body[2] == 'x') {
+        if (ty->dtype == DCF_I1) return;  // bit-packed in MLIR's raw form
+        // Point into the source text: the attribute text lives in op->props.
+        const std::string* src = op->prop(key);
+        const size_t a = src->find("\"0x") + 3, b = src->find('"', a);
+        d->hex = std::string_view(src->data() + a, b - a);
+        const uint64_t bytes = d->hex.size() / 2;
+        if (bytes == d->es) {
+          d->splat = true;
+          d->n = 1;
+        } else if (bytes == (uint64_t)ty->count() * d->es) {
+          d->n = (uint64_t)ty->count();
+        } else {
+          return;
+        }
+      } else if (!body.empty() && body[0] == '(') {
+        return;  // complex
+      } else {
+        std::vector<std::string> toks;
+        flatten_list(body, toks);
+        const bool list = !body.empty() && body[0] == '[';
+        if (!list && toks.size() == 1) {
+          d->splat = true;
+        } else if ((int64_t)toks.size() != ty->count()) {
+          return;
+        }
+        d->n = toks.size();
+        d->host.resize(d->n * d->es);
+        for (size_t i = 0; i < toks.size(); i++) {
+          uint64_t bits;
+          if (!encode(toks[i], &bits)) return;
+          memcpy(d->host.data() + i * d->es, &bits, d->es);
+        }
+      }
+    } else {
+      if (ty->shaped()) return;
+      uint64_t bits;
+      if (!encode(lit, &bits)) return;
+      d->splat = true;
+      d->n = 1;
+      d->host.resize(d->es);
+      memcpy(d->host.data(), &bits, d->es);
+    }
+    op->cst = d;
+    op->cst_text = true;
+  }
+};
+
+}  // namespace
+
+std::unique_ptr<Module> parse_module(const std::string& text) {
+  auto m = std::make_unique<Module>();
+  Parser p(text, *m);
+  m->top = p.parse_top();
+  return m;
+}
+
+// =================================================================== print
+
+namespace {
+
+class Printer {
+ public:
+  Printer(const PrintHooks& h) : h_(h) {}
+  std::string out;
+
+  void op(Op* o, int indent) {
+    out.append(indent, ' ');
+    if (!o->results.empty()) {
+      const int base = next_++;
+      const std::string name = "%" + std::to_string(base);
+      for (size_t i = 0; i < o->results.size(); i++)
+        names_[o->results[i]] = o->results.size() == 1 ? name : name + "#" + std::to_string(i);
+      out += name;
+      if (o->results.size() > 1) out += ":" + std::to_string(o->results.size());
+      out += " = ";
+    }
+    out += "\"" + o->name + "\"(";
+    for (size_t i = 0; i < o->operands.size(); i++) {
+      if (i) out += ", ";
+      out += name_of(o->operands[i]);
+    }
+    out += ")";
+    if (!o->successors.empty()) out += o->successors;
+    if (!o->props.empty() || (o->cst && !o->cst_text && !o->cst->poison)) {
+      out += " <{";
+      bool first = true;
+      const char* key = o->name == "tosa.const" ? "values" : "value";
+      bool wrote_value = false;
+      for (auto& kv : o->props) {
+        if (!first) out += ", ";
+        first = false;
+        out += kv.first;
+        if (o->cst && !o->cst_text && kv.first == key) {
+          out += " = " + value_text(*o->cst);
+          wrote_value = true;
+        } else if (!kv.second.empty()) {
+          out += " = " + kv.second;
+        }
+      }
+      if (o->cst && !o->cst_text && !wrote_value && !o->cst->poison) {
+        if (!first) out += ", ";
+        out += std::string(key) + " = " + value_text(*o->cst);
+      }
+      out += "}>";
+    }
+    const bool isolated = o->name == "func.func" || o->name == "builtin.module";
+    if (!o->regions.empty()) {
+      out += " (";
+      for (size_t r = 0; r < o->regions.size(); r++) {
+        if (r) out += ", ";
+        int saved_next = next_, saved_arg = arg_;
+        if (isolated) next_ = 0, arg_ = 0;
+        region(o->regions[r], indent);
+        if (isolated) next_ = saved_next, arg_ = saved_arg;
+      }
+      out += ")";
+    }
+    if (!o->attrs.empty()) out += " " + o->attrs;
+    out += " : (";
+    for (size_t i = 0; i < o->operands.size(); i++) {
+      if (i) out += ", ";
+      out += o->operands[i]->ty->text;
+    }
+    out += ") -> ";
+    if (o->results.size() == 1 && o->results[0]->ty->text.find("->") == std::string::npos) {
+      out += o->results[0]->ty->text;
+    } else {
+      out += "(";
+      for (size_t i = 0; i < o->results.size(); i++) {
+        if (i) out += ", ";
+        out += o->results[i]->ty->text;
+      }
+      out += ")";
+    }
+    if (!o->loc.empty()) out += " " + o->loc;
+    out += "\n";
+  }
+
+ private:
+  const PrintHooks& h_;
+  std::unordered_map<Value*, std::string> names_;
+  int next_ = 0, arg_ = 0;
+
+  std::string name_of(Value* v) {
+    auto it = names_.find(v);
+    if (it != names_.end()) return it->second;
+    return "%<undefined>";
+  }
+
+  void region(Region* r, int indent) {
+    out += "{\n";
+    for (size_t bi = 0; bi < r->blocks.size(); bi++) {
+      Block* b = r->blocks[bi];
+      for (Value* a : b->args) names_[a] = "%arg" + std::to_string(arg_++);
+      if (!b->args.empty() || bi > 0) {
+        out.append(indent, ' ');
+        out += b->label.empty() ? "^bb" + std::to_string(bi) : b->label;
+        if (!b->args.empty()) {
+          out += "(";
+          for (size_t i = 0; i < b->args.size(); i++) {
+            if (i) out += ", ";
+            out += names_[b->args[i]] + ": " + b->args[i]->ty->text;
+          }
+          out += ")";
+        }
+        out += ":\n";
+      }
+      for (Op* o : b->ops) op(o, indent + 2);
+    }
+    out.append(indent, ' ');
+    out += "}";
+  }
+
+  std::string value_text(DenseValue& v) {
+    const bool is_float = v.ty->is_float();
+    auto scalar = [&](uint64_t bits) {
+      return is_float ? print_float_literal(bits, v.dtype) : print_int_literal(bits, v.dtype);
+    };
+    if (!v.elements) {
+      const uint64_t bits = h_.bits0_of(v, h_.ctx);
+      if (v.dtype == DCF_I1) return scalar(bits);
+      return scalar(bits) + " : " + v.ty->text;
+    }
+    if (v.splat) return "dense<" + scalar(h_.bits0_of(v, h_.ctx)) + "> : " + v.ty->text;
+    // mlir-opt prints up to 100 elements as a literal list and larger
+    // attributes as the hex of their raw bytes.  MLIR's raw i1 data is
+    // bit-packed, so i1 is always printed as a list here.
+    if (v.n <= 100 || v.dtype == DCF_I1) {
+      const std::string hex = h_.hex_of(v, h_.ctx);
+      std::string s = "dense<";
+      // nested brackets follow the shape
+      // block[d]: elements in one list at nesting depth d
+      const std::vector<int64_t>& shape = v.ty->shape;
+      std::vector<uint64_t> block(shape.size(), 1);
+      for (int i = (int)shape.size() - 1; i >= 0; i--)
+        block[i] = (uint64_t)shape[i] * (i + 1 < (int)shape.size() ? block[i + 1] : 1);
+      for (uint64_t e = 0; e < v.n; e++) {
+        for (size_t d = 0; d < shape.size(); d++)
+          if (e % block[d] == 0) s += "[";
+        uint64_t bits = 0;
+        for (size_t b = 0; b < v.es; b++) {
+          const auto nib = [&](char c) { return (uint64_t)(c <= '9' ? c - '0' : c - 'A' + 10); };
+          bits |= ((nib(hex[2 * (e * v.es + b)]) << 4) | nib(hex[2 * (e * v.es + b) + 1])) << (8 * b);
+        }
+        s += scalar(bits);
+        for (size_t d = shape.size(); d-- > 0;)
+          if ((e + 1) % block[d] == 0) s += "]";
+        if (e + 1 < v.n) s += ", ";
+      }
+      return s + "> : " + v.ty->text;
+    }
+    return "dense<\"0x" + h_.hex_of(v, h_.ctx) + "\"> : " + v.ty->text;
+  }
+};
+
+}  // namespace
+
+std::string print_module(Module& m, const PrintHooks& hooks) {
+  Printer p(hooks);
+  p.op(m.top, 0);
+  return p.out;
+}
+
+}  // namespace dco

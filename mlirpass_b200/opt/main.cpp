@@ -1,0 +1,201 @@
+// main.cpp — the C ABI (include/dcfold_opt.h) and the `dcfold-opt` command
+// line of the pass driver.
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <iostream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "../../include/dcfold_opt.h"
+#include "engine.h"
+#include "fold.h"
+#include "ir.h"
+
+namespace {
+
+thread_local std::string g_opt_err;
+
+using Clock = std::chrono::steady_clock;
+double ms_since(Clock::time_point t) { return std::chrono::duration<double, std::milli>(Clock::now() - t).count(); }
+
+struct Engines {
+  std::vector<std::unique_ptr<dco::Engine>> own;
+  std::vector<dco::Engine*> list;
+  explicit Engines(int n) {
+    if (n == 0) {  // host-only
+      own.push_back(std::make_unique<dco::Engine>(-1));
+      list.push_back(own.back().get());
+      return;
+    }
+    int visible = 0;
+    if (cudaGetDeviceCount(&visible) != cudaSuccess || visible <= 0)
+      throw std::runtime_error("no CUDA device available; dcfold-opt has no CPU fallback");
+    if (n <= 0 || n > visible) n = visible;
+    for (int i = 0; i < n; i++) {
+      own.push_back(std::make_unique<dco::Engine>(i));
+      list.push_back(own.back().get());
+    }
+  }
+  dco::Engine* of(const dco::DenseValue& v) {
+    if (v.dev)
+      for (auto* e : list)
+        if (e->device() == v.dev->device) return e;
+    return list[0];
+  }
+};
+
+std::string hex_hook(dco::DenseValue& v, void* ctx) { return ((Engines*)ctx)->of(v)->hex_of(v); }
+uint64_t bits_hook(dco::DenseValue& v, void* ctx) { return ((Engines*)ctx)->of(v)->bits0_of(v); }
+
+std::vector<std::string> split_chunks(const std::string& text, bool split) {
+  std::vector<std::string> out;
+  if (!split) {
+    out.push_back(text);
+    return out;
+  }
+  size_t a = 0;
+  for (;;) {
+    const size_t b = text.find("// -----", a);
+    out.push_back(text.substr(a, b == std::string::npos ? std::string::npos : b - a));
+    if (b == std::string::npos) break;
+    const size_t nl = text.find('\n', b);
+    a = nl == std::string::npos ? text.size() : nl + 1;
+  }
+  return out;
+}
+
+std::string run_all(const std::string& text, const std::string& pipeline, int n_gpus, bool split,
+                    dcf_opt_stats* st) {
+  Engines eng(n_gpus);
+  std::string result;
+  dcf_opt_stats total{};
+  const auto chunks = split_chunks(text, split);
+  for (size_t i = 0; i < chunks.size(); i++) {
+    auto t0 = Clock::now();
+    std::unique_ptr<dco::Module> m = dco::parse_module(chunks[i]);
+    total.parse_ms += ms_since(t0);
+    t0 = Clock::now();
+    dco::PassStats ps;
+    dco::run_pipeline(*m, pipeline, eng.list, &ps);
+    dco::fetch_results(*m, eng.list);
+    total.run_ms += ms_since(t0);
+    total.folds += ps.folds;
+    total.refused += ps.refused;
+    t0 = Clock::now();
+    dco::PrintHooks hooks;
+    hooks.hex_of = hex_hook;
+    hooks.bits0_of = bits_hook;
+    hooks.ctx = &eng;
+    if (i) result += "// -----\n";
+    result += dco::print_module(*m, hooks);
+    total.print_ms += ms_since(t0);
+  }
+  for (auto* e : eng.list) {
+    total.h2d_bytes += e->stats.h2d_bytes;
+    total.d2h_bytes += e->stats.d2h_bytes;
+    total.batches += e->stats.batches;
+  }
+  if (st) *st = total;
+  return result;
+}
+
+}  // namespace
+
+extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int split_input_file,
+                           char** out, size_t* out_len, dcf_opt_stats* stats) {
+  if (!text || !pipeline || !out) {
+    g_opt_err = "null argument";
+    return -1;
+  }
+  try {
+    std::string r = run_all(std::string(text, len), pipeline, n_gpus, split_input_file != 0, stats);
+    char* p = (char*)malloc(r.size() + 1);
+    if (!p) {
+      g_opt_err = "out of memory";
+      return -3;
+    }
+    memcpy(p, r.data(), r.size());
+    p[r.size()] = 0;
+    *out = p;
+    if (out_len) *out_len = r.size();
+    return 0;
+  } catch (const std::exception& e) {
+    g_opt_err = e.what();
+    return -1;
+  }
+}
+
+extern "C" void dcf_opt_free(char* p) { free(p); }
+
+extern "C" const char* dcf_opt_last_error(void) { return g_opt_err.c_str(); }
+
+#ifdef DCFOLD_OPT_MAIN
+int main(int argc, char** argv) {
+  std::string input = "-", output = "-", pipeline;
+  int gpus = 1;
+  bool split = false, timing = false;
+  for (int i = 1; i < argc; i++) {
+    std::string a = argv[i];
+    if (a == "--canonicalize" || a == "-canonicalize" || a.rfind("--canonicalize=", 0) == 0 ||
+        a.rfind("-canonicalize=", 0) == 0)
+      pipeline = "canonicalize";
+    else if (a.rfind("--pass-pipeline=", 0) == 0 || a.rfind("-pass-pipeline=", 0) == 0)
+      pipeline = a.substr(a.find('=') + 1);
+    else if (a == "--split-input-file" || a == "-split-input-file")
+      split = true;
+    else if (a.rfind("--gpus=", 0) == 0)
+      gpus = atoi(a.c_str() + 7);
+    else if (a == "--timing")
+      timing = true;
+    else if (a == "-o" && i + 1 < argc)
+      output = argv[++i];
+    else if (a.rfind("--mlir-", 0) == 0 || a.rfind("-mlir-", 0) == 0 || a == "--allow-unregistered-dialect")
+      continue;  // printing flags: the output is always generic form
+    else if (a[0] != '-' || a == "-")
+      input = a;
+    else {
+      fprintf(stderr, "dcfold-opt: unknown option %s\n", a.c_str());
+      return 2;
+    }
+  }
+  if (pipeline.empty()) {
+    fprintf(stderr, "usage: dcfold-opt [--canonicalize | --pass-pipeline=...] [--gpus=N] [--split-input-file] "
+                    "[--timing] [-o out] [in.mlir]\n");
+    return 2;
+  }
+  std::stringstream buf;
+  if (input == "-") buf << std::cin.rdbuf();
+  else {
+    std::ifstream f(input, std::ios::binary);
+    if (!f) {
+      fprintf(stderr, "dcfold-opt: cannot read %s\n", input.c_str());
+      return 1;
+    }
+    buf << f.rdbuf();
+  }
+  const std::string text = buf.str();
+  dcf_opt_stats st{};
+  try {
+    std::string r = run_all(text, pipeline, gpus, split, &st);
+    if (output == "-") fwrite(r.data(), 1, r.size(), stdout);
+    else {
+      std::ofstream f(output, std::ios::binary);
+      f.write(r.data(), (std::streamsize)r.size());
+    }
+  } catch (const std::exception& e) {
+    fprintf(stderr, "dcfold-opt: %s\n", e.what());
+    return 1;
+  }
+  if (timing)
+    fprintf(stderr,
+            "{\"parse_ms\": %.3f, \"run_ms\": %.3f, \"print_ms\": %.3f, \"folds\": %llu, \"refused\": %llu, "
+            "\"h2d_bytes\": %llu, \"d2h_bytes\": %llu, \"batches\": %llu}\n",
+            st.parse_ms, st.run_ms, st.print_ms, st.folds, st.refused, st.h2d_bytes, st.d2h_bytes, st.batches);
+  return 0;
+}
+#endif

@@ -1,0 +1,191 @@
+"""The pass driver on a B200: whole pipelines on MLIR text.
+
+Every golden case (a fold op over constants from the reference's fixtures)
+becomes a function and runs through `canonicalize`; the returned value must
+be the fixture's folded constant, or the op left in place.  Then the fold
+configurations run end to end through `--canonicalize` and
+`builtin.module(func.func(tosa-layerwise-constant-fold,canonicalize))`, and
+every resulting constant is compared bit for bit with the oracle.
+"""
+import numpy as np
+import pytest
+
+from golden_cases import CANON, SIZE, STORAGE, case_id, load_cases
+from mlir_text import parse_funcs
+from mlirpass_b200 import mlir_gen, opt
+from mlirpass_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+CASES = load_cases()
+
+
+def ty_text(o):
+    if o["shape"] is None:
+        return o["dtype"]
+    return f'{o["kind"]}<{"x".join(str(d) for d in o["shape"])}x{o["dtype"]}>'
+
+
+def literal(o):
+    dt = CANON.get(o["dtype"], o["dtype"])
+    bits = [int(b, 16) for b in o["bits"]]
+    isf = dt.startswith("f") or dt == "bf16"
+    def one(b):
+        if isf:
+            return "0x%0*X" % (2 * SIZE[dt], b)
+        if dt == "i1":
+            return "true" if b else "false"
+        w = 8 * SIZE[dt]
+        return str(b - (1 << w) if b >> (w - 1) else b)
+    if o["shape"] is None:
+        return one(bits[0]) if dt == "i1" else f"{one(bits[0])} : {ty_text(o)}"
+    if o["splat"]:
+        return f"dense<{one(bits[0])}> : {ty_text(o)}"
+    raw = np.array(bits, dtype=STORAGE[SIZE[dt]]).tobytes().hex().upper()
+    return f'dense<"0x{raw}"> : {ty_text(o)}'
+
+
+def render(c):
+    lines, names = [], []
+    dialect = c["op"].split(".")[0]
+    for i, o in enumerate(c["operands"]):
+        op, key = ("tosa.const", "values") if dialect == "tosa" else ("arith.constant", "value")
+        ty = ty_text(o)
+        lines.append(f'    %{i} = "{op}"() <{{{key} = {literal(o)}}}> : () -> {ty}')
+        names.append(f"%{i}")
+    props = dict(c["props"])
+    p = ", ".join(f"{k} = {v}" for k, v in props.items())
+    rty = ty_text(c["result"])
+    ins = ", ".join(ty_text(o) for o in c["operands"])
+    args = ", ".join(names)
+    if c["op"] == "tosa.transpose":
+        args, ins = names[0], ty_text(c["operands"][0])
+    lines.append(f'    %r = "{c["op"]}"({args}){" <{" + p + "}>" if p else ""} : ({ins}) -> {rty}')
+    return ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> {rty}, sym_name = "t"}}> ({{\n' + "\n".join(lines) +
+            f'\n    "func.return"(%r) : ({rty}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
+
+
+@pytest.mark.parametrize("case", CASES, ids=[case_id(c) for c in CASES])
+def test_golden_through_canonicalize(case):
+    out, _ = opt.run(render(case), "canonicalize")
+    f = parse_funcs(out)["t"]
+    d = f.defs.get(f.ret.operands[0])
+    exp = case["expected"]
+    if exp["status"] == "not_folded":
+        assert d is not None and d.name == case["op"], out
+        return
+    assert d is not None and d.const is not None, out
+    want = [int(x, 16) for x in exp["bits"]]
+    got = d.const.bits
+    if exp["splat"]:
+        assert set(got) == {want[0]}, (got, want)
+    else:
+        assert got == want, (got, want)
+
+
+def consts_returned(out, name="main"):
+    f = parse_funcs(out)[name]
+    res = []
+    for v in f.ret.operands:
+        d = f.defs.get(v)
+        res.append(d)
+    return res
+
+
+def full(d, n):
+    """Values of a parsed constant, expanded if it was printed as a splat."""
+    a = np.array(d.const.bits, dtype=np.uint64)
+    return np.full(n, a[0], dtype=np.uint64) if d.const.splat else a
+
+
+def test_config1_pipeline(oracle):
+    out, st = opt.run(mlir_gen.config1_text(), "canonicalize")
+    (d,) = consts_returned(out)
+    c = W.config1()
+    want = oracle.binary("addf", "f32", c["A"], c["B"]).out
+    assert d.name == "arith.constant" and np.array_equal(full(d, want.size), want.astype(np.uint64))
+    assert st["folds"] == 1 and st["run_ms"] > 0
+
+
+def test_config2_chain_pipeline(oracle):
+    out, st = opt.run(mlir_gen.config2_text(1024), "canonicalize")
+    (d,) = consts_returned(out)
+    c = W.config2(1024)
+    env = {k: c[k] for k in "ABCD"}
+    for op, a, b, t in W.CHAIN2:
+        env[t] = oracle.binary(op, "f32", env[a], env[b]).out.view(np.float32)
+    assert np.array_equal(full(d, 1 << 20), env["t6"].view(np.uint32).astype(np.uint64))
+    assert st["folds"] == 6
+    f = parse_funcs(out)["main"]
+    assert [o.name for o in f.ops] == ["arith.constant", "func.return"]
+
+
+@pytest.mark.parametrize("dt", ["i8", "i32", "i64"])
+def test_config3_pipeline(dt, oracle):
+    rows, cols = 1024, 512
+    out, st = opt.run(mlir_gen.config3_text(dt, rows, cols), "canonicalize")
+    res = consts_returned(out)
+    c = W.config3(dt, rows, cols)
+    n = rows * cols
+    expect = [("addi", "X", "Y"), ("muli", "X", "Y"), ("subi", "X", "Y"), ("andi", "X", "Y"), ("xori", "X", "Y"),
+              ("shli", "X", "S"), ("divsi", "Xd", "Yd"), ("remsi", "Xd", "Yd")]
+    for d, (op, a, b) in zip(res, expect):
+        want = oracle.binary(op, dt, c[a], c[b])
+        if want.folded:
+            assert d.name == "arith.constant", op
+            assert np.array_equal(full(d, n), want.out.astype(np.uint64)), op
+        else:
+            assert d.name == "arith." + op, op   # divsi refuses on INT_MIN / -1
+    assert res[6].name == "arith.divsi" and res[7].name == "arith.constant"
+
+
+@pytest.mark.parametrize("prerounded", [False, True])
+def test_config4_pipeline(prerounded, oracle):
+    n = 1 << 20
+    out, st = opt.run(mlir_gen.config4_text(n, prerounded), "canonicalize")
+    t1, t2, e1, e2, si, fp, c1, c2 = consts_returned(out)
+    c = W.config4(n, prerounded)
+    assert c1.name == "arith.cmpf" and c2.name == "arith.cmpf"      # dense cmpf never folds
+    want_si = oracle.convert("fptosi", "f32", "i32", c["inrange"]).out
+    assert np.array_equal(full(si, n), want_si.astype(np.uint64))
+    want_fp = oracle.convert("sitofp", "i32", "f32", c["ints"]).out
+    assert np.array_equal(full(fp, n), want_fp.astype(np.uint64))
+    tb = oracle.convert("truncf", "f32", "bf16", c["x"])
+    assert (t1.name == "arith.constant") == tb.folded
+    if prerounded:
+        assert np.array_equal(full(t1, n), tb.out.astype(np.uint64))
+        # extf(truncf(x)) folds back to x
+        assert np.array_equal(full(e1, n), c["x"].astype(np.uint64))
+    else:
+        assert t1.name == "arith.truncf" and e1.name == "arith.extf"
+
+
+def test_config5_layerwise_pipeline(oracle):
+    funcs, side, ws = 24, 64, 512
+    out, st = opt.run(mlir_gen.config5_text(funcs, side, ws), mlir_gen.LAYERWISE)
+    fs = parse_funcs(out)
+    for i in range(funcs):
+        a, b = W.config5_func(i, side)
+        t1 = oracle.binary("addf", "f32", a, b).out
+        t2 = oracle.binary("mulf", "f32", t1, a).out
+        r = oracle.reciprocal("f32", t2).out
+        f = fs[f"f{i}"]
+        d = f.defs.get(f.ret.operands[0])
+        assert d.name == "tosa.const", f"f{i}"
+        assert np.array_equal(full(d, side * side), r.astype(np.uint64)), f"f{i}"
+        assert [o.name for o in f.ops] == ["tosa.const", "func.return"]
+    w = W.config5_weight(ws)
+    f = fs["weights"]
+    d = f.defs.get(f.ret.operands[0])
+    assert d.name == "tosa.const"
+    assert np.array_equal(full(d, ws * ws), w.reshape(ws, ws).T.reshape(-1).astype(np.uint64))
+
+
+def test_canonicalize_alone_leaves_non_splat_tosa_folds():
+    # The reference's canonicalize folds tosa.reciprocal / transpose only for
+    # splat inputs: with non-splat constants the ops stay.
+    out, st = opt.run(mlir_gen.config5_text(2, 8, 64), "builtin.module(func.func(canonicalize))")
+    fs = parse_funcs(out)
+    assert any(o.name == "tosa.reciprocal" for o in fs["f0"].ops)
+    assert any(o.name == "tosa.transpose" for o in fs["weights"].ops)
