@@ -392,6 +392,130 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------- per-configuration kernels
+
+def run_kernels(args):
+    """Every configuration's fold kernels on device-resident operands: one
+    JSON line per kernel with its time and fraction of the HBM roof."""
+    import torch
+    import mlirpass_b200 as dcf
+    from mlirpass_b200 import workloads as W
+
+    torch.cuda.set_device(0)
+    os.environ["DCF_DEVICES"] = "0"
+    dcf.init(1)
+    dev = torch.device("cuda", 0)
+    peak, _ = load_peaks()
+    flush = torch.ones(32 << 20, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    st = torch.empty(2, dtype=torch.int64, device=dev)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    def timeit(launch, nbytes, label, reps=None):
+        reps = reps or args.steps
+        times = []
+        for r in range(args.warmup + reps):
+            flush.sum()
+            dcf.status_reset(st, stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if r >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"workload": label[0], "fold": label[1], "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                "frac": round(gbs / peak, 3), "bytes": nbytes}
+        print(json.dumps(line), flush=True)
+
+    # config 1 / 2 (f32 binary)
+    c1 = W.config1()
+    a, b = T(c1["A"]), T(c1["B"])
+    o = torch.empty_like(a)
+    timeit(lambda: dcf.binary_async("addf", "f32", a, b, o, st), 12 * a.numel(), ("config1 1024x1024 f32", "addf"))
+    # config 3 (integers)
+    for dt in ("i8", "i32", "i64"):
+        c = W.config3(dt)
+        X, Y, S, Xd, Yd = (T(c[k].view({"i8": np.int8, "i32": np.int32, "i64": np.int64}[dt]))
+                           for k in ("X", "Y", "S", "Xd", "Yd"))
+        o = torch.empty_like(X)
+        es = X.element_size()
+        for op, l, r in (("addi", X, Y), ("muli", X, Y), ("subi", X, Y), ("andi", X, Y), ("xori", X, Y),
+                         ("shli", X, S), ("divsi", Xd, Yd), ("remsi", Xd, Yd)):
+            timeit(lambda op=op, l=l, r=r: dcf.binary_async(op, dt, l, r, o, st), 3 * es * X.numel(),
+                   (f"config3 8192x2048 {dt}", op))
+    # config 4 (conversions)
+    c = W.config4()
+    cp = W.config4(prerounded=True)
+    x, xr, inr, ints = T(c["x"]), T(cp["x"]), T(c["inrange"]), T(c["ints"])
+    n = x.numel()
+    o16 = torch.empty(n, dtype=torch.int16, device=dev)
+    o32 = torch.empty(n, dtype=torch.int32, device=dev)
+    o8 = torch.empty(n, dtype=torch.uint8, device=dev)
+    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->bf16 (refuses)"))
+    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", xr, o16, st), 6 * n, ("config4b 16M", "truncf f32->bf16"))
+    timeit(lambda: dcf.convert_async("truncf", "f32", "f16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->f16 (refuses)"))
+    timeit(lambda: dcf.convert_async("extf", "bf16", "f32", o16, o32, st), 6 * n, ("config4b 16M", "extf bf16->f32"))
+    timeit(lambda: dcf.convert_async("fptosi", "f32", "i32", inr, o32, st), 8 * n, ("config4 16M", "fptosi f32->i32"))
+    timeit(lambda: dcf.convert_async("sitofp", "i32", "f32", ints, o32, st), 8 * n, ("config4 16M", "sitofp i32->f32"))
+    timeit(lambda: dcf.binary_async("cmpf", "f32", x, inr, o8, st, flags=4 << 8), 9 * n,
+           ("config4 16M", "cmpf olt (kernel only; dense cmpf is not folded)"))
+    # config 5: 4096 functions per step, batched; and the 16384^2 bf16 transpose
+    funcs = [W.config5_func(i) for i in range(args.funcs)]
+    A = [T(f[0]) for f in funcs]
+    B = [T(f[1]) for f in funcs]
+    O = [torch.empty_like(t) for t in A]
+
+    def batched(op, unary=False):
+        for k in range(0, len(A), dcf.NOALLOC_MAX_JOBS):
+            jobs = [{"op": op, "dtype": "f32", "lhs": A[i], "out": O[i], **({} if unary else {"rhs": B[i]})}
+                    for i in range(k, min(k + dcf.NOALLOC_MAX_JOBS, len(A)))]
+            dcf.batch_noalloc(jobs, stream)
+    per = A[0].numel()
+    timeit(lambda: batched("addf"), 12 * per * len(A), (f"config5 {len(A)} funcs 256x256", "addf (batched)"), reps=5)
+    timeit(lambda: batched("reciprocal", True), 8 * per * len(A), (f"config5 {len(A)} funcs 256x256", "reciprocal (batched)"), reps=5)
+    w = T(W.config5_weight().view(np.int16))
+    wo = torch.empty_like(w)
+    timeit(lambda: dcf.transpose2d_async(2, 16384, 16384, w, wo), 4 * w.numel(), ("config5 16384x16384 bf16", "transpose"))
+
+
+def run_pass(args):
+    """A whole pipeline through the pass driver on MLIR text: parse / run /
+    print phases, like the reference's own bench (fuzz/src/bench.rs:55-66)."""
+    from mlirpass_b200 import mlir_gen as G
+    from mlirpass_b200 import opt
+    cfg = args.workload.split(":", 1)[1]
+    if cfg == "config1":
+        text, pipe = G.config1_text(), "canonicalize"
+    elif cfg == "config2":
+        text, pipe = G.config2_text(), "canonicalize"
+    elif cfg.startswith("config3"):
+        text, pipe = G.config3_text(cfg.split("-")[1] if "-" in cfg else "i32"), "canonicalize"
+    elif cfg == "config4":
+        text, pipe = G.config4_text(), "canonicalize"
+    elif cfg == "config4b":
+        text, pipe = G.config4_text(prerounded=True), "canonicalize"
+    elif cfg == "config5":
+        text, pipe = G.config5_text(args.funcs), G.LAYERWISE
+    else:
+        raise SystemExit(f"unknown workload {args.workload}")
+    runs = []
+    for r in range(max(1, args.warmup) + args.steps):
+        out, st = opt.run(text, pipe, n_gpus=args.gpus)
+        if r >= max(1, args.warmup):
+            runs.append(st)
+    best = min(runs, key=lambda s: s["run_ms"])
+    line = {"workload": f"pass {cfg}", "pipeline": pipe, "n_gpus": args.gpus, "text_bytes": len(text),
+            "parse_ms": round(best["parse_ms"], 2), "run_ms": round(best["run_ms"], 3),
+            "run_ms_mean": round(statistics.mean(s["run_ms"] for s in runs), 3),
+            "print_ms": round(best["print_ms"], 2), "folds": best["folds"], "refused": best["refused"],
+            "h2d_bytes": best["h2d_bytes"], "d2h_bytes": best["d2h_bytes"], "batches": best["batches"],
+            "runs": len(runs)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,9 +524,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="chain4096",
+                    help="chain4096 (the headline line), kernels, or pass:<config1|config2|config3-i8|...|config5>")
+    ap.add_argument("--funcs", type=int, default=4096, help="functions of config 5")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "kernels":
+        run_kernels(args)
+        return
+    if args.workload.startswith("pass:"):
+        run_pass(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -61,7 +61,9 @@ def run(text: str | bytes, pipeline: str, n_gpus: int = 1, split_input_file: boo
     if rc != 0:
         raise OptError(lib().dcf_opt_last_error().decode())
     try:
-        s = ctypes.string_at(out, n.value).decode()
+        # ctypes.string_at takes a C int size: copy through a sized array so
+        # outputs above 2 GiB work.
+        s = bytes((ctypes.c_char * n.value).from_address(out.value)).decode() if n.value else ""
     finally:
         lib().dcf_opt_free(out)
     return s, st.as_dict()

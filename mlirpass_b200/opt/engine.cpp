@@ -3,7 +3,11 @@
 
 #include <chrono>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <stdexcept>
+#include <thread>
+#include <tuple>
 
 namespace dco {
 
@@ -39,16 +43,79 @@ constexpr size_t kSmallHex = 8192;
 
 }  // namespace
 
+namespace {
+
+struct Pool {
+  std::mutex mu;
+  std::multimap<size_t, void*> free[64];
+  static size_t size_class(size_t n) {
+    if (n <= 256) return 256;
+    if (n <= (64u << 10)) {
+      size_t c = 512;
+      while (c < n) c <<= 1;
+      return c;
+    }
+    return (n + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
+  }
+};
+
+Pool& pool() {
+  static Pool* p = new Pool;  // outlives every DeviceBuf
+  return *p;
+}
+
+// Run fn(0..n-1) on n threads and wait (n small: a copy split in parts).
+template <class F>
+void parallel(int n, F&& fn) {
+  if (n <= 1) {
+    fn(0);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int i = 1; i < n; i++) th.emplace_back([&, i] { fn(i); });
+  fn(0);
+  for (auto& t : th) t.join();
+}
+
+void copy_parallel(void* dst, const void* src, size_t bytes) {
+  const int parts = bytes >= (8u << 20) ? 4 : 1;
+  parallel(parts, [&](int i) {
+    const size_t a = bytes * (size_t)i / parts, b = bytes * (size_t)(i + 1) / parts;
+    memcpy((char*)dst + a, (const char*)src + a, b - a);
+  });
+}
+
+}  // namespace
+
 DeviceBuf::DeviceBuf(int dev, size_t n) : bytes(n), device(dev) {
+  cap = Pool::size_class(n);
+  Pool& p = pool();
+  {
+    std::lock_guard<std::mutex> g(p.mu);
+    auto it = p.free[dev & 63].find(cap);
+    if (it != p.free[dev & 63].end()) {
+      ptr = it->second;
+      p.free[dev & 63].erase(it);
+      return;
+    }
+  }
   ck(cudaSetDevice(dev), "cudaSetDevice");
-  ck(cudaMalloc(&ptr, n < 16 ? 16 : n), "cudaMalloc");
+  cudaError_t e = cudaMalloc(&ptr, cap);
+  if (e != cudaSuccess) {
+    // Give cached blocks back to the driver and try once more.
+    cudaGetLastError();
+    std::lock_guard<std::mutex> g(p.mu);
+    for (auto& kv : p.free[dev & 63]) cudaFree(kv.second);
+    p.free[dev & 63].clear();
+    ck(cudaMalloc(&ptr, cap), "cudaMalloc");
+  }
 }
 
 DeviceBuf::~DeviceBuf() {
-  if (ptr) {
-    cudaSetDevice(device);
-    cudaFree(ptr);
-  }
+  if (!ptr) return;
+  Pool& p = pool();
+  std::lock_guard<std::mutex> g(p.mu);
+  p.free[device & 63].emplace(cap, ptr);
 }
 
 Engine::Engine(int device) : dev_(device) {
@@ -64,6 +131,74 @@ Engine::~Engine() {
     cudaStreamSynchronize(s_);
     cudaStreamDestroy(s_);
   }
+  for (int k = 0; k < kSlots; k++) {
+    if (pinned_[k]) cudaFreeHost(pinned_[k]);
+    if (slot_ev_[k]) cudaEventDestroy(slot_ev_[k]);
+  }
+}
+
+void Engine::ensure_pinned() {
+  if (pinned_[0]) return;
+  for (int k = 0; k < kSlots; k++) {
+    ck(cudaHostAlloc(&pinned_[k], kSlotBytes, cudaHostAllocPortable), "cudaHostAlloc");
+    ck(cudaEventCreateWithFlags(&slot_ev_[k], cudaEventDisableTiming), "cudaEventCreate");
+  }
+}
+
+void Engine::upload(void* dst, const void* src, size_t bytes) {
+  set_device();
+  stats.h2d_bytes += bytes;
+  if (bytes < (1u << 20)) {
+    ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s_), "H2D");
+    sync();
+    return;
+  }
+  ensure_pinned();
+  bool used[kSlots] = {false};
+  size_t off = 0;
+  int k = 0;
+  while (off < bytes) {
+    const size_t n = std::min(kSlotBytes, bytes - off);
+    if (used[k]) ck(cudaEventSynchronize(slot_ev_[k]), "cudaEventSynchronize");
+    copy_parallel(pinned_[k], (const char*)src + off, n);
+    ck(cudaMemcpyAsync((char*)dst + off, pinned_[k], n, cudaMemcpyHostToDevice, s_), "H2D");
+    ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
+    used[k] = true;
+    off += n;
+    k = (k + 1) % kSlots;
+  }
+  sync();
+}
+
+void Engine::download(void* dst, const void* src, size_t bytes) {
+  set_device();
+  stats.d2h_bytes += bytes;
+  if (bytes < (1u << 20)) {
+    ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s_), "D2H");
+    sync();
+    return;
+  }
+  ensure_pinned();
+  size_t pend_off[kSlots] = {0}, pend_n[kSlots] = {0};
+  size_t off = 0;
+  int k = 0;
+  auto drain = [&](int j) {
+    if (!pend_n[j]) return;
+    ck(cudaEventSynchronize(slot_ev_[j]), "cudaEventSynchronize");
+    copy_parallel((char*)dst + pend_off[j], pinned_[j], pend_n[j]);
+    pend_n[j] = 0;
+  };
+  while (off < bytes) {
+    const size_t n = std::min(kSlotBytes, bytes - off);
+    drain(k);
+    ck(cudaMemcpyAsync(pinned_[k], (const char*)src + off, n, cudaMemcpyDeviceToHost, s_), "D2H");
+    ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
+    pend_off[k] = off;
+    pend_n[k] = n;
+    off += n;
+    k = (k + 1) % kSlots;
+  }
+  for (int j = 0; j < kSlots; j++) drain((k + j) % kSlots);
 }
 
 void Engine::set_device() {
@@ -92,13 +227,10 @@ void Engine::to_device(DenseValue& v) {
   const uint64_t bytes = v.bytes();
   auto buf = std::make_shared<DeviceBuf>(dev_, bytes);
   if (!v.host.empty()) {
-    ck(cudaMemcpyAsync(buf->ptr, v.host.data(), bytes, cudaMemcpyHostToDevice, s_), "H2D");
-    stats.h2d_bytes += bytes;
-    sync();
+    upload(buf->ptr, v.host.data(), bytes);
   } else if (!v.hex.empty()) {
     DeviceBuf text(dev_, v.hex.size());
-    ck(cudaMemcpyAsync(text.ptr, v.hex.data(), v.hex.size(), cudaMemcpyHostToDevice, s_), "H2D hex");
-    stats.h2d_bytes += v.hex.size();
+    upload(text.ptr, v.hex.data(), v.hex.size());
     if (!aux_) aux_ = std::make_unique<DeviceBuf>(dev_, sizeof(dcf_status));
     dcf_status* st = (dcf_status*)aux_->ptr;
     check(dcf_status_reset_async(st, s_), "status reset");
@@ -126,9 +258,7 @@ void Engine::to_host(DenseValue& v) {
   if (!v.dev) to_device(v);
   set_device();
   v.host.resize(v.bytes());
-  ck(cudaMemcpyAsync(v.host.data(), v.dev->ptr, v.bytes(), cudaMemcpyDeviceToHost, s_), "D2H");
-  sync();
-  stats.d2h_bytes += v.bytes();
+  download(v.host.data(), v.dev->ptr, v.bytes());
 }
 
 uint64_t Engine::bits0_of(DenseValue& v) {
@@ -162,9 +292,7 @@ std::string Engine::hex_of(DenseValue& v) {
     DeviceBuf text(dev_, 2 * bytes);
     check(dcf_hex_encode_async(v.dev->ptr, bytes, (char*)text.ptr, s_), "hex encode");
     std::string s(2 * bytes, '0');
-    ck(cudaMemcpyAsync(&s[0], text.ptr, 2 * bytes, cudaMemcpyDeviceToHost, s_), "D2H hex");
-    sync();
-    stats.d2h_bytes += 2 * bytes;
+    download(&s[0], text.ptr, 2 * bytes);
     return s;
   }
   to_host(v);
@@ -232,32 +360,80 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
   };
 
   std::vector<std::shared_ptr<DeviceBuf>> outs(R);
+  std::vector<const void*> ls(R, nullptr), rs(R, nullptr);
   for (size_t i = 0; i < R; i++) {
     FoldRequest& q = *reqs[i];
-    const void* l = q.lhs ? operand(*q.lhs, spos[i].first) : nullptr;
-    const void* r = q.rhs ? operand(*q.rhs, spos[i].second) : nullptr;
+    ls[i] = q.lhs ? operand(*q.lhs, spos[i].first) : nullptr;
+    rs[i] = q.rhs ? operand(*q.rhs, spos[i].second) : nullptr;
+    if (q.kind != FoldRequest::SPLAT_SCAN)
+      outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * dcf_dtype_size((dcf_dtype)q.out_dtype));
+  }
+  // Many small folds of one kind (one per isolated function, say) go out as
+  // one launch per group through the batched kernel.
+  std::vector<bool> batched(R, false);
+  std::vector<dcf_status> bst(R);
+  {
+    std::map<std::tuple<int, int, int, int, uint32_t>, std::vector<size_t>> groups;
+    for (size_t i = 0; i < R; i++) {
+      const FoldRequest& q = *reqs[i];
+      if ((q.kind == FoldRequest::BINARY || q.kind == FoldRequest::CONVERT || q.kind == FoldRequest::RECIPROCAL) &&
+          q.n <= (4u << 20))
+        groups[{(int)q.kind, q.op, q.dtype, q.out_dtype, q.flags}].push_back(i);
+    }
+    for (auto& [key, idx] : groups) {
+      if (idx.size() < 8) continue;
+      for (size_t a = 0; a < idx.size(); a += 1024) {
+        const size_t b = std::min(idx.size(), a + 1024);
+        std::vector<dcf_job> jobs(b - a);
+        for (size_t t = a; t < b; t++) {
+          const FoldRequest& q = *reqs[idx[t]];
+          dcf_job& j = jobs[t - a];
+          memset(&j, 0, sizeof j);
+          j.op = q.kind == FoldRequest::RECIPROCAL ? DCF_RECIPROCAL : (uint32_t)q.op;
+          j.dtype = (uint32_t)q.dtype;
+          j.out_dtype = (uint32_t)q.out_dtype;
+          j.flags = q.flags;
+          j.lhs = ls[idx[t]];
+          j.rhs = q.kind == FoldRequest::BINARY ? rs[idx[t]] : nullptr;
+          j.out = outs[idx[t]]->ptr;
+          j.n = q.n;
+          j.lhs_splat = q.lhs->splat;
+          j.rhs_splat = q.kind == FoldRequest::BINARY ? q.rhs->splat : 0;
+        }
+        check(dcf_batch_noalloc(jobs.data(), jobs.size(), s_), "batched fold");
+        for (size_t t = a; t < b; t++) {
+          const dcf_result& r = jobs[t - a].result;
+          bst[idx[t]].first_fail = r.first_fail_index;
+          bst[idx[t]].splat_word = r.is_splat ? 1u : 0u;
+          bst[idx[t]].error = 0xFFFFFFFFu;
+          batched[idx[t]] = true;
+        }
+      }
+    }
+  }
+  for (size_t i = 0; i < R; i++) {
+    if (batched[i]) continue;
+    FoldRequest& q = *reqs[i];
+    const void* l = ls[i];
+    const void* r = rs[i];
     set_device();
     const size_t oes = dcf_dtype_size((dcf_dtype)q.out_dtype);
     switch (q.kind) {
       case FoldRequest::BINARY:
-        outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * oes);
         check(dcf_binary_async((dcf_op)q.op, (dcf_dtype)q.dtype, l, q.lhs->splat, r, q.rhs->splat, q.n, q.flags,
                                outs[i]->ptr, st + i, s_),
               "binary fold");
         break;
       case FoldRequest::CONVERT:
-        outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * oes);
         check(dcf_convert_async((dcf_op)q.op, (dcf_dtype)q.dtype, (dcf_dtype)q.out_dtype, l, q.lhs->splat, q.n,
                                 q.flags, outs[i]->ptr, st + i, s_),
               "convert fold");
         break;
       case FoldRequest::RECIPROCAL:
-        outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * oes);
         check(dcf_reciprocal_async((dcf_dtype)q.dtype, l, q.lhs->splat, q.n, q.flags, outs[i]->ptr, st + i, s_),
               "reciprocal fold");
         break;
       case FoldRequest::PERMUTE:
-        outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * oes);
         check(dcf_permute_async(oes, (int)q.shape.size(), q.shape.data(), q.perms.data(), l, outs[i]->ptr, s_),
               "transpose fold");
         break;
@@ -269,6 +445,8 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
   std::vector<dcf_status> hst(R);
   ck(cudaMemcpyAsync(hst.data(), st, R * sizeof(dcf_status), cudaMemcpyDeviceToHost, s_), "D2H status");
   sync();
+  for (size_t i = 0; i < R; i++)
+    if (batched[i]) hst[i] = bst[i];
   // First element of every all-equal result, fetched together.
   std::vector<uint64_t> first(R, 0);
   bool any = false;
@@ -306,6 +484,8 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     } else {
       d->n = q.n;
       d->dev = outs[i];
+      // The kernel's splat test already said the values differ.
+      if (q.kind != FoldRequest::PERMUTE) d->all_equal = 0;
     }
     if (q.kind == FoldRequest::PERMUTE && q.lhs->all_equal == 1) d->all_equal = 1;
     q.out = d;

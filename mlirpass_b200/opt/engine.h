@@ -20,6 +20,9 @@
 
 namespace dco {
 
+// Device memory from a per-device caching pool: freed buffers are kept by
+// size class and handed out again, so a fold chain reuses the same HBM
+// instead of calling cudaMalloc / cudaFree for every intermediate.
 class DeviceBuf {
  public:
   DeviceBuf(int device, size_t bytes);
@@ -28,6 +31,7 @@ class DeviceBuf {
   DeviceBuf& operator=(const DeviceBuf&) = delete;
   void* ptr = nullptr;
   size_t bytes = 0;
+  size_t cap = 0;
   int device = 0;
 };
 
@@ -78,12 +82,26 @@ class Engine {
 
   EngineStats stats;
 
+  // Host <-> device copies of `bytes` (synchronous).  Large copies from
+  // pageable memory go through pinned staging slots, filled and emptied by
+  // several host threads while the copy engine moves the previous slot.
+  void upload(void* dst, const void* src, size_t bytes);
+  void download(void* dst, const void* src, size_t bytes);
+
  private:
   int dev_;
   cudaStream_t s_ = nullptr;
   std::unique_ptr<DeviceBuf> status_;   // dcf_status slots of a batch
   size_t status_cap_ = 0;
   std::unique_ptr<DeviceBuf> aux_;      // status word of uploads and scans outside a batch
+  static constexpr int kSlots = 4;
+  static constexpr size_t kSlotBytes = 16u << 20;
+  void* pinned_[kSlots] = {nullptr};
+  cudaEvent_t slot_ev_[kSlots] = {nullptr};
+  void ensure_pinned();
+  void run_batched(const std::vector<FoldRequest*>& reqs, const std::vector<const void*>& ls,
+                   const std::vector<const void*>& rs, std::vector<std::shared_ptr<DeviceBuf>>& outs,
+                   std::vector<dcf_status>& hst);
   void set_device();
   void check(int rc, const char* what);
   void sync();

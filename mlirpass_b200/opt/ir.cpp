@@ -348,6 +348,9 @@ static bool parse_int_literal(const std::string& tok, int dtype, uint64_t* bits)
 
 namespace {
 
+// Property values longer than this are not copied out of the parsed text.
+constexpr size_t kBigProp = 4096;
+
 [[noreturn]] void fail(const std::string& msg, size_t at) {
   throw std::runtime_error("parse error at offset " + std::to_string(at) + ": " + msg);
 }
@@ -454,6 +457,13 @@ class Parser {
 
   // A balanced span starting here, ending before a top-level char in `stops`.
   std::string span(const char* stops) {
+    const auto r = span_pos(stops);
+    return trim(s_.substr(r.first, r.second - r.first));
+  }
+
+  // The same, as [start, end) offsets: nothing is copied, and string
+  // literals (the hex payload of a dense constant) are skipped with memchr.
+  std::pair<size_t, size_t> span_pos(const char* stops) {
     ws();
     const size_t start = p_;
     int depth = 0;
@@ -461,8 +471,19 @@ class Parser {
     for (; p_ < s_.size(); p_++) {
       const char c = s_[p_];
       if (str) {
-        if (c == '\\') p_++;
-        else if (c == '"') str = false;
+        if (c == '\\') {
+          p_++;
+          continue;
+        }
+        if (c == '"') {
+          str = false;
+          continue;
+        }
+        const void* q = memchr(s_.data() + p_, '"', s_.size() - p_);
+        const void* bs = memchr(s_.data() + p_, '\\', q ? (size_t)((const char*)q - (s_.data() + p_)) : s_.size() - p_);
+        if (q && !bs) {
+          p_ = (size_t)((const char*)q - s_.data()) - 1;  // land on the quote next iteration
+        }
         continue;
       }
       if (depth == 0 && strchr(stops, c)) break;
@@ -474,7 +495,10 @@ class Parser {
         depth--;
       }
     }
-    return trim(s_.substr(start, p_ - start));
+    size_t a = start, b = p_;
+    while (a < b && isspace((unsigned char)s_[a])) a++;
+    while (b > a && isspace((unsigned char)s_[b - 1])) b--;
+    return {a, b};
   }
 
   std::string ident() {
@@ -631,14 +655,27 @@ class Parser {
       op->successors = s_.substr(a, p_ - a);
     }
     if (eat("<{")) {
-      std::string body = span("}");
+      while (!peek('}')) {
+        const auto r = span_pos(",}");
+        const size_t eq = s_.find('=', r.first);
+        if (eq == std::string::npos || eq >= r.second) {
+          op->props.emplace_back(trim(s_.substr(r.first, r.second - r.first)), "");
+        } else {
+          std::string key = trim(s_.substr(r.first, eq - r.first));
+          size_t va = eq + 1;
+          while (va < r.second && isspace((unsigned char)s_[va])) va++;
+          if (r.second - va > kBigProp) {
+            op->big_key = key;
+            op->big_value = std::string_view(s_.data() + va, r.second - va);
+            op->props.emplace_back(std::move(key), "");
+          } else {
+            op->props.emplace_back(std::move(key), s_.substr(va, r.second - va));
+          }
+        }
+        if (!eat(',')) break;
+      }
       expect('}');
       expect('>');
-      for (auto& entry : split_top(body, ',')) {
-        const size_t eq = entry.find('=');
-        if (eq == std::string::npos) op->props.emplace_back(trim(entry), "");
-        else op->props.emplace_back(trim(entry.substr(0, eq)), trim(entry.substr(eq + 1)));
-      }
     }
     const bool isolated = op->name == "func.func" || op->name == "builtin.module";
     if (peek("({")) {
@@ -727,6 +764,29 @@ class Parser {
     if (!key || op->results.size() != 1) return;
     const std::string* text = op->prop(key);
     if (!text) return;
+    const std::string_view full = (op->big_key == key) ? op->big_value : std::string_view(*text);
+    // Big literals: only the ends are examined here; the hex body is
+    // decoded (on the GPU) when the constant is first used.
+    if (full.size() > kBigProp) {
+      const size_t colon = full.rfind(" : ");
+      const size_t q0 = full.find("\"0x"), q1 = full.rfind('"');
+      if (colon == std::string_view::npos || q0 == std::string_view::npos || q1 <= q0 || full.substr(0, 6) != "dense<")
+        return;
+      TypeP ty = type_of(std::string(full.substr(colon + 3)));
+      if (!ty->dtype || !ty->static_shape() || ty->dtype == DCF_I1) return;
+      auto d = std::make_shared<DenseValue>();
+      d->ty = ty;
+      d->dtype = ty->dtype;
+      d->es = elem_bytes(ty->dtype);
+      d->elements = true;
+      d->hex = full.substr(q0 + 3, q1 - q0 - 3);
+      const uint64_t bytes = d->hex.size() / 2;
+      if (bytes != (uint64_t)ty->count() * d->es) return;
+      d->n = (uint64_t)ty->count();
+      op->cst = d;
+      op->cst_text = true;
+      return;
+    }
     std::string lit = *text, ty_text;
     // split "literal : type" at the last top-level " : "
     {
@@ -848,6 +908,9 @@ class Printer {
         if (o->cst && !o->cst_text && kv.first == key) {
           out += " = " + value_text(*o->cst);
           wrote_value = true;
+        } else if (kv.first == o->big_key && !o->big_value.empty()) {
+          out += " = ";
+          out.append(o->big_value.data(), o->big_value.size());
         } else if (!kv.second.empty()) {
           out += " = " + kv.second;
         }
@@ -970,10 +1033,23 @@ class Printer {
 
 }  // namespace
 
+// An upper estimate of the printed size, so the output grows without
+// reallocating (and re-copying) the big literals.
+static size_t estimate(const Op* o) {
+  size_t n = 256 + o->big_value.size() + o->attrs.size();
+  for (auto& kv : o->props) n += kv.first.size() + kv.second.size() + 4;
+  if (o->cst && !o->cst_text) n += 2 * o->cst->bytes() + 64;
+  for (const Region* r : o->regions)
+    for (const Block* b : r->blocks)
+      for (const Op* in : b->ops) n += estimate(in);
+  return n;
+}
+
 std::string print_module(Module& m, const PrintHooks& hooks) {
   Printer p(hooks);
+  p.out.reserve(estimate(m.top));
   p.op(m.top, 0);
-  return p.out;
+  return std::move(p.out);
 }
 
 }  // namespace dco

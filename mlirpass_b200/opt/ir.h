@@ -89,6 +89,10 @@ struct Op {
   std::vector<Value*> operands;
   std::vector<Value*> results;
   std::vector<std::pair<std::string, std::string>> props;  // <{...}> entries, text
+  // A property value too large to copy (a dense literal of a big constant)
+  // is kept as a view into the parsed text; its props entry holds "".
+  std::string big_key;
+  std::string_view big_value;
   std::string attrs;          // "{...}" discardable attributes, verbatim
   std::string successors;     // "[...]" verbatim
   std::vector<Region*> regions;

@@ -92,7 +92,8 @@ std::string run_all(const std::string& text, const std::string& pipeline, int n_
     hooks.bits0_of = bits_hook;
     hooks.ctx = &eng;
     if (i) result += "// -----\n";
-    result += dco::print_module(*m, hooks);
+    if (chunks.size() == 1) result = dco::print_module(*m, hooks);
+    else result += dco::print_module(*m, hooks);
     total.print_ms += ms_since(t0);
   }
   for (auto* e : eng.list) {
