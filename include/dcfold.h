@@ -78,6 +78,9 @@ typedef enum dcf_op {
   DCF_MINIMUMF = 6,
   DCF_MAXNUMF = 7,
   DCF_MINNUMF = 8,
+  /* remf: the exact IEEE remainder of truncating division (fmod), the
+   * closure `x % y` of src/patterns/arith/canonicalize.rs:387 */
+  DCF_REMF = 9,
   /* integer binary (src/patterns/arith/canonicalize.rs:277-325, 469-683) */
   DCF_ADDI = 16,
   DCF_SUBI = 17,
@@ -96,10 +99,23 @@ typedef enum dcf_op {
   DCF_MAXUI = 30,
   DCF_MINSI = 31,
   DCF_MINUI = 32,
+  /* rounding divisions (src/patterns/arith/canonicalize.rs:287-317,
+   * 557-595): refuse on a zero divisor and on signed overflow */
+  DCF_CEILDIVUI = 33,
+  DCF_CEILDIVSI = 34,
+  DCF_FLOORDIVSI = 35,
+  /* high half of the double-width product: the second result of
+   * mulsi_extended / mului_extended (canonicalize.rs:928-949); the low half
+   * is DCF_MULI */
+  DCF_MULSI_HI = 36,
+  DCF_MULUI_HI = 37,
   /* compares producing i1 bytes (src/patterns/arith/canonicalize.rs:94-130,
    * 791-839); the predicate goes in the flags (DCF_FLAG_PRED) */
   DCF_CMPI = 48,
   DCF_CMPF = 49,
+  /* carry bit of addui_extended (canonicalize.rs:878-893): i1 bytes,
+   * (a + b mod 2^w) <u a.  The borrow of subui_extended is DCF_CMPI ult. */
+  DCF_ADDUI_CARRY = 50,
   /* unary conversions (src/patterns/arith/canonicalize.rs:400-434, 717-762) */
   DCF_EXTF = 64,
   DCF_TRUNCF = 65,
@@ -107,6 +123,15 @@ typedef enum dcf_op {
   DCF_UITOFP = 67,
   DCF_FPTOSI = 68,
   DCF_FPTOUI = 69,
+  /* more unary element maps through dcf_convert: negf (sign flip,
+   * canonicalize.rs:327-333), flush_denormals (:69-77, :376-385), and the
+   * integer width changes extsi / extui / trunci (:388-398, :685-706; also
+   * index_cast / index_castui, :435-454, with index as i64) */
+  DCF_NEGF = 70,
+  DCF_FLUSH_DENORMALS = 71,
+  DCF_EXTSI = 72,
+  DCF_EXTUI = 73,
+  DCF_TRUNCI = 74,
   /* tosa.reciprocal, 1/x round-to-nearest-even
    * (src/patterns/tosa/canonicalize.rs:596-605; layerwise pass) */
   DCF_RECIPROCAL = 80
@@ -216,8 +241,9 @@ int dcf_binary(dcf_op op, dcf_dtype dtype, const void* lhs, int lhs_splat,
                void* out, dcf_result* res);
 
 /* Elementwise conversion fold (extf, truncf, sitofp, uitofp, fptosi,
- * fptoui) from `from` to `to`.  Replaces the Const::map closures at
- * src/patterns/arith/canonicalize.rs:402-434 and 727-742. */
+ * fptoui, negf, flush_denormals, extsi, extui, trunci) from `from` to
+ * `to`.  Replaces the Const::map closures at
+ * src/patterns/arith/canonicalize.rs:327-333, 376-434, 685-762. */
 int dcf_convert(dcf_op op, dcf_dtype from, dcf_dtype to, const void* in,
                 int in_splat, uint64_t n, uint32_t flags, void* out,
                 dcf_result* res);
@@ -227,6 +253,15 @@ int dcf_convert(dcf_op op, dcf_dtype from, dcf_dtype to, const void* in,
  * element step of the layerwise reciprocal fold. */
 int dcf_reciprocal(dcf_dtype dtype, const void* in, int in_splat, uint64_t n,
                    uint32_t flags, void* out, dcf_result* res);
+
+/* Elementwise select over dense constants: out[i] = cond[i] != 0 ? t[i] :
+ * f[i], with i1 condition bytes and values of elem_size bytes (1, 2, 4 or
+ * 8); a splat operand holds one element.  Never refuses.  Replaces the
+ * value loop of Folder::select (src/patterns/arith/canonicalize.rs:869-875);
+ * the shortcuts before it (:842-868) stay in the caller. */
+int dcf_select(size_t elem_size, const void* cond, int cond_splat,
+               const void* t, int t_splat, const void* f, int f_splat,
+               uint64_t n, void* out, dcf_result* res);
 
 /* Permute a dense row-major tensor of `rank` dims: out has shape
  * in_shape[perms[i]].  elem_size is 1, 2, 4 or 8 bytes.  Rank 2 with
@@ -296,6 +331,11 @@ int dcf_convert_async(dcf_op op, dcf_dtype from, dcf_dtype to, const void* in,
 int dcf_reciprocal_async(dcf_dtype dtype, const void* in, int in_splat,
                          uint64_t n, uint32_t flags, void* out,
                          dcf_status* status, void* stream);
+
+int dcf_select_async(size_t elem_size, const void* cond, int cond_splat,
+                     const void* t, int t_splat, const void* f, int f_splat,
+                     uint64_t n, void* out, dcf_status* status,
+                     void* stream);
 
 /* 2-D transpose of a rows x cols row-major matrix on device pointers. */
 int dcf_transpose2d_async(size_t elem_size, uint64_t rows, uint64_t cols,

@@ -27,6 +27,10 @@ typedef struct dcf_opt_stats {
                         bringing every folded constant back to host memory */
   double print_ms;   /* IR -> text */
   unsigned long long folds, refused, h2d_bytes, d2h_bytes, batches;
+  /* parts of run_ms, summed over the GPUs: packing constants into the
+   * pinned staging slots and copying them in (with their decode), the fold
+   * launches and their statuses, and bringing results back to the host */
+  double upload_ms, fold_ms, download_ms;
 } dcf_opt_stats;
 
 /* Run `pipeline` ("canonicalize", or "builtin.module(func.func(P,...))" with

@@ -35,14 +35,21 @@ STORAGE = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
 
 OPS = {
     "addf": 1, "subf": 2, "mulf": 3, "divf": 4, "maximumf": 5, "minimumf": 6, "maxnumf": 7, "minnumf": 8,
+    "remf": 9,
     "addi": 16, "subi": 17, "muli": 18, "andi": 19, "ori": 20, "xori": 21, "shli": 22, "shrui": 23,
     "shrsi": 24, "divsi": 25, "divui": 26, "remsi": 27, "remui": 28, "maxsi": 29, "maxui": 30,
-    "minsi": 31, "minui": 32, "cmpi": 48, "cmpf": 49,
+    "minsi": 31, "minui": 32, "ceildivui": 33, "ceildivsi": 34, "floordivsi": 35, "mulsi_hi": 36,
+    "mului_hi": 37, "cmpi": 48, "cmpf": 49, "addui_carry": 50,
     "extf": 64, "truncf": 65, "sitofp": 66, "uitofp": 67, "fptosi": 68, "fptoui": 69,
+    "negf": 70, "flush_denormals": 71, "extsi": 72, "extui": 73, "trunci": 74,
     "reciprocal": 80,
 }
 BINARY_OPS = tuple(k for k, v in OPS.items() if v < 64)
-CONVERT_OPS = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui")
+FLOAT_BINARY_OPS = tuple(k for k, v in OPS.items() if v < 16 or k == "cmpf")
+INT_BINARY_OPS = tuple(k for k in BINARY_OPS if k not in FLOAT_BINARY_OPS)
+BOOL_RESULT_OPS = ("cmpi", "cmpf", "addui_carry")
+CONVERT_OPS = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "negf", "flush_denormals", "extsi",
+               "extui", "trunci")
 
 FLAG_PRED_SHIFT = 8
 FLAG_NEG_DEFAULT_NAN = 1 << 16
@@ -92,6 +99,7 @@ SIGNATURES = {
     "dcf_binary": (_I, [_I, _I, _VP, _I, _VP, _I, _U64, _U32, _VP, _RP]),
     "dcf_convert": (_I, [_I, _I, _I, _VP, _I, _U64, _U32, _VP, _RP]),
     "dcf_reciprocal": (_I, [_I, _VP, _I, _U64, _U32, _VP, _RP]),
+    "dcf_select": (_I, [_SZ, _VP, _I, _VP, _I, _VP, _I, _U64, _VP, _RP]),
     "dcf_transpose": (_I, [_SZ, _I, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _VP, _VP, _RP]),
     "dcf_hex_encode": (_I, [_VP, _U64, _VP]),
     "dcf_hex_decode": (_I, [_VP, _U64, _VP]),
@@ -102,6 +110,7 @@ SIGNATURES = {
     "dcf_binary_async": (_I, [_I, _I, _VP, _I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
     "dcf_convert_async": (_I, [_I, _I, _I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
     "dcf_reciprocal_async": (_I, [_I, _VP, _I, _U64, _U32, _VP, _VP, _VP]),
+    "dcf_select_async": (_I, [_SZ, _VP, _I, _VP, _I, _VP, _I, _U64, _VP, _VP, _VP]),
     "dcf_transpose2d_async": (_I, [_SZ, _U64, _U64, _VP, _VP, _VP]),
     "dcf_permute_async": (_I, [_SZ, _I, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _VP, _VP,
                                _VP]),
@@ -185,7 +194,7 @@ def binary(op: str, dtype: str, lhs, rhs, *, n: int | None = None, lhs_splat: bo
     l, r = as_storage(lhs, dtype), as_storage(rhs, dtype)
     if n is None:
         n = 1 if (lhs_splat and rhs_splat) else max(len(l), len(r))
-    odt = "i1" if op in ("cmpi", "cmpf") else dtype
+    odt = "i1" if op in BOOL_RESULT_OPS else dtype
     if out is None:
         out = np.empty(n, dtype=storage(odt))
     res = Result()
@@ -217,6 +226,25 @@ def reciprocal(dtype: str, x, *, n: int | None = None, splat: bool = False, flag
         out = np.empty(n, dtype=storage(dtype))
     res = Result()
     _check(lib().dcf_reciprocal(DTYPES[dtype], _ptr(a), int(splat), n, flags, _ptr(out), ctypes.byref(res)))
+    return Fold(bool(res.folded), bool(res.is_splat), int(res.first_fail_index), out)
+
+
+def select(cond, t, f, *, n: int | None = None, cond_splat: bool = False, t_splat: bool = False,
+           f_splat: bool = False, out: np.ndarray | None = None) -> Fold:
+    """Elementwise select over dense constants (Folder::select's value loop):
+    out[i] = t[i] if cond[i] else f[i].  t and f share one storage dtype."""
+    c = np.ascontiguousarray(cond, dtype=np.uint8).reshape(-1)
+    a = np.ascontiguousarray(t).reshape(-1)
+    b = np.ascontiguousarray(f).reshape(-1)
+    if a.dtype.itemsize != b.dtype.itemsize:
+        raise ValueError("t and f must have the same element size")
+    if n is None:
+        n = max(len(c), len(a), len(b))
+    if out is None:
+        out = np.empty(n, dtype=a.dtype)
+    res = Result()
+    _check(lib().dcf_select(a.dtype.itemsize, _ptr(c), int(cond_splat), _ptr(a), int(t_splat), _ptr(b),
+                            int(f_splat), n, _ptr(out), ctypes.byref(res)))
     return Fold(bool(res.folded), bool(res.is_splat), int(res.first_fail_index), out)
 
 
@@ -267,7 +295,7 @@ def batch(jobs: list[dict]) -> list[Fold]:
     outs = []
     for i, j in enumerate(jobs):
         op, dt = j["op"], j["dtype"]
-        odt = j.get("out_dtype") or ("i1" if op in ("cmpi", "cmpf") else dt)
+        odt = j.get("out_dtype") or ("i1" if op in BOOL_RESULT_OPS else dt)
         l = as_storage(j["lhs"], dt)
         r = as_storage(j["rhs"], dt) if "rhs" in j else None
         n = j.get("n") or max(len(l), len(r) if r is not None else 0)
@@ -302,10 +330,19 @@ def batch_noalloc(jobs: list[dict], stream=None) -> list[Fold]:
     [flags].  At most NOALLOC_MAX_JOBS jobs per call; overlapping calls on
     the GPU race on the library's one scratch array.
     """
+    arr = device_jobs(jobs)
+    run_device_jobs(arr, stream)
+    return [Fold(bool(arr[i].result.folded), bool(arr[i].result.is_splat), int(arr[i].result.first_fail_index),
+                 None) for i in range(len(jobs))]
+
+
+def device_jobs(jobs: list[dict]):
+    """The ctypes job table of batch_noalloc, built once so that a caller can
+    run the same batch repeatedly (run_device_jobs)."""
     arr = (Job * len(jobs))()
     for i, j in enumerate(jobs):
         op, dt = j["op"], j["dtype"]
-        odt = j.get("out_dtype") or ("i1" if op in ("cmpi", "cmpf") else dt)
+        odt = j.get("out_dtype") or ("i1" if op in BOOL_RESULT_OPS else dt)
         arr[i].op, arr[i].dtype, arr[i].out_dtype = OPS[op], DTYPES[dt], DTYPES[odt]
         arr[i].flags = j.get("flags", 0)
         arr[i].lhs = _tptr(j["lhs"])
@@ -314,9 +351,12 @@ def batch_noalloc(jobs: list[dict], stream=None) -> list[Fold]:
         arr[i].n = j.get("n") or j["out"].numel()
         arr[i].lhs_splat = int(j.get("lhs_splat", False))
         arr[i].rhs_splat = int(j.get("rhs_splat", False))
-    _check(lib().dcf_batch_noalloc(arr, len(jobs), _stream(stream)))
-    return [Fold(bool(arr[i].result.folded), bool(arr[i].result.is_splat), int(arr[i].result.first_fail_index),
-                 None) for i in range(len(jobs))]
+    return arr
+
+
+def run_device_jobs(arr, stream=None) -> None:
+    """dcf_batch_noalloc on a table from device_jobs; results land in it."""
+    _check(lib().dcf_batch_noalloc(arr, len(arr), _stream(stream)))
 
 def _tptr(t) -> int:
     return t.data_ptr()
@@ -356,6 +396,14 @@ def reciprocal_async(dtype: str, x, out, status, *, n: int | None = None, splat:
         n = out.numel()
     _check(lib().dcf_reciprocal_async(DTYPES[dtype], _tptr(x), int(splat), n, flags, _tptr(out), _tptr(status),
                                       _stream(stream)))
+
+
+def select_async(cond, t, f, out, status, *, n: int | None = None, cond_splat: bool = False, t_splat: bool = False,
+                 f_splat: bool = False, stream=None) -> None:
+    if n is None:
+        n = out.numel()
+    _check(lib().dcf_select_async(out.element_size(), _tptr(cond), int(cond_splat), _tptr(t), int(t_splat), _tptr(f),
+                                  int(f_splat), n, _tptr(out), _tptr(status), _stream(stream)))
 
 
 def transpose2d_async(elem_size: int, rows: int, cols: int, x, out, stream=None) -> None:

@@ -23,7 +23,11 @@ LIB = os.path.join(PKG, "libdcfold.so")
 ORACLE_SRC = os.path.join(ROOT, "oracle", "dcf_oracle.c")
 ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libdcforacle.so")
 
-SOURCES = ["dcf_ew_float.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_misc.cu", "dcf_runtime.cu", "dcf_noalloc.cu"]
+# The float and conversion kernel families are split by layout so that the
+# (template-heavy) translation units compile in parallel.
+SOURCES = ["dcf_ew_float.cu", "dcf_ew_float_f32.cu", "dcf_ew_float_f64.cu", "dcf_ew_float_h.cu",
+           "dcf_ew_float_f8.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_ew_convert_ff.cu",
+           "dcf_ew_convert_if.cu", "dcf_ew_convert_fi.cu", "dcf_misc.cu", "dcf_runtime.cu", "dcf_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -402,6 +402,45 @@ __device__ __forceinline__ bool int_op(uint64_t a, uint64_t b, uint64_t& out) {
     else out = ua % ub;
     return true;
   }
+  else if constexpr (OP == DCF_CEILDIVUI) {                  // canonicalize.rs:287-298
+    if (ub == 0) return false;
+    out = (ua / ub + (ua % ub != 0 ? 1 : 0)) & I::MASK;
+    return true;
+  }
+  else if constexpr (OP == DCF_CEILDIVSI) {                  // ceildivsi, :557-595
+    // Every overflow flag of the reference's steps is raised exactly when
+    // an operand is the signed minimum (and the dividend is not zero).
+    if (ub == 0) return false;
+    const int64_t sa = I::sx(ua), sb = I::sx(ub);
+    if (sa == 0) { out = 0; return true; }
+    const int64_t smin = (W == 64) ? (int64_t)0x8000000000000000ull : -(int64_t)(1ull << (W - 1));
+    if (sa == smin || sb == smin) return false;
+    int64_t q = sa / sb;
+    if (sa % sb != 0 && ((sa > 0) == (sb > 0))) q += 1;
+    out = (uint64_t)q & I::MASK;
+    return true;
+  }
+  else if constexpr (OP == DCF_FLOORDIVSI) {                 // :306-317
+    if (ub == 0) return false;
+    const int64_t sa = I::sx(ua), sb = I::sx(ub);
+    const int64_t smin = (W == 64) ? (int64_t)0x8000000000000000ull : -(int64_t)(1ull << (W - 1));
+    if (sa == smin && sb == -1) return false;
+    int64_t q = sa / sb;
+    const int64_t r = sa % sb;
+    if (r != 0 && ((r < 0) != (sb < 0))) q -= 1;
+    out = (uint64_t)q & I::MASK;
+    return true;
+  }
+  else if constexpr (OP == DCF_MULSI_HI) {                   // mul_extended, :939-944
+    if constexpr (W == 64) out = (uint64_t)__mul64hi((long long)ua, (long long)ub);
+    else out = (uint64_t)((I::sx(ua) * I::sx(ub)) >> W) & I::MASK;
+    return true;
+  }
+  else if constexpr (OP == DCF_MULUI_HI) {
+    if constexpr (W == 64) out = (uint64_t)__umul64hi(ua, ub);
+    else out = ((ua * ub) >> W) & I::MASK;
+    return true;
+  }
   else if constexpr (OP == DCF_MAXSI) { out = I::sx(ua) > I::sx(ub) ? ua : ub; return true; }
   else if constexpr (OP == DCF_MAXUI) { out = ua > ub ? ua : ub; return true; }
   else if constexpr (OP == DCF_MINSI) { out = I::sx(ua) < I::sx(ub) ? ua : ub; return true; }
@@ -425,6 +464,39 @@ template <int W> __device__ __forceinline__ uint8_t cmpi(int pred, uint64_t a, u
     case 8: return ua > ub;
     default: return ua >= ub;
   }
+}
+
+// addui_extended's overflow bit (canonicalize.rs:887-891): sum <u lhs.
+template <int W> __device__ __forceinline__ uint8_t add_carry(uint64_t a, uint64_t b) {
+  using I = IntW<W>;
+  const uint64_t ua = a & I::MASK;
+  return ((ua + (b & I::MASK)) & I::MASK) < ua;
+}
+
+// remf, `x % y` (canonicalize.rs:387): the remainder of truncating
+// division, which is always exact, so computing it in a wider format and
+// narrowing back loses nothing.  NaN operands propagate quieted (first one
+// wins); inf % y and x % 0 are invalid and give the default NaN.
+template <class L> __device__ __forceinline__ uint64_t remf(uint64_t a, uint64_t b, uint64_t dnan) {
+  if (is_nan<L>(a) || is_nan<L>(b)) return nan_result<L>(a, b, dnan);
+  if (is_inf<L>(a) || is_zero<L>(b)) return dnan;
+  if (is_inf<L>(b) || is_zero<L>(a)) return a;
+  if constexpr (L::B == 8) {
+    return (uint64_t)__double_as_longlong(fmod(__longlong_as_double((long long)a), __longlong_as_double((long long)b)));
+  } else if constexpr (L::B == 4 || L::E + L::M == 15) {
+    return from_f32_rn<L>(fmodf(to_f32<L>(a), to_f32<L>(b)));
+  } else {
+    const float x = __uint_as_float((uint32_t)convert_rn<L, F32L>(a));
+    const float y = __uint_as_float((uint32_t)convert_rn<L, F32L>(b));
+    return convert_rn<F32L, L>(__float_as_uint(fmodf(x, y)));
+  }
+}
+
+// flush_denormal (canonicalize.rs:69-77): a subnormal becomes the zero of
+// its sign; everything else is kept.
+template <class L> __device__ __forceinline__ uint64_t flush_denormal(uint64_t b) {
+  if ((b & L::EXPM) == 0 && (b & L::MANT) != 0) return b & L::SIGN;
+  return b;
 }
 
 // --------------------------------------------------------- conversions

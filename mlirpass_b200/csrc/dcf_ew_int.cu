@@ -1,13 +1,45 @@
 // dcf_ew_int.cu — integer binary folds (wraparound ApInt arithmetic, the
-// refusing ops shli/shrui/shrsi, divsi/divui, remsi/remui) and dense cmpi.
+// refusing ops shli/shrui/shrsi, div / rem / ceildiv / floordiv, the high
+// half of mul*_extended), dense cmpi and the carry of addui_extended.
 #include "dcf_kernels.cuh"
 
 namespace dcf {
+
+// The ops that have a lane-wise form on packed 8- and 16-bit words (none
+// of them refuses an element).
+template <int OP, int W> constexpr bool word_op() {
+  return (W == 8 || W == 16) && (OP == DCF_ADDI || OP == DCF_SUBI || OP == DCF_ANDI || OP == DCF_ORI ||
+                                 OP == DCF_XORI || OP == DCF_MAXSI || OP == DCF_MAXUI || OP == DCF_MINSI ||
+                                 OP == DCF_MINUI);
+}
 
 template <int OP, int W> struct IOp {
   using In = typename IntW<W>::T;
   using Out = typename IntW<W>::T;
   static constexpr bool kBinary = true;
+  static constexpr bool kWord = word_op<OP, W>();
+  // Four i8 (two i16) lanes per word: the video SIMD intrinsics wrap per
+  // lane, as the element closures do.
+  __device__ static __forceinline__ uint32_t word(uint32_t a, uint32_t b) {
+    if constexpr (OP == DCF_ANDI) return a & b;
+    else if constexpr (OP == DCF_ORI) return a | b;
+    else if constexpr (OP == DCF_XORI) return a ^ b;
+    else if constexpr (W == 8) {
+      if constexpr (OP == DCF_ADDI) return __vadd4(a, b);
+      else if constexpr (OP == DCF_SUBI) return __vsub4(a, b);
+      else if constexpr (OP == DCF_MAXSI) return __vmaxs4(a, b);
+      else if constexpr (OP == DCF_MAXUI) return __vmaxu4(a, b);
+      else if constexpr (OP == DCF_MINSI) return __vmins4(a, b);
+      else return __vminu4(a, b);
+    } else {
+      if constexpr (OP == DCF_ADDI) return __vadd2(a, b);
+      else if constexpr (OP == DCF_SUBI) return __vsub2(a, b);
+      else if constexpr (OP == DCF_MAXSI) return __vmaxs2(a, b);
+      else if constexpr (OP == DCF_MAXUI) return __vmaxu2(a, b);
+      else if constexpr (OP == DCF_MINSI) return __vmins2(a, b);
+      else return __vminu2(a, b);
+    }
+  }
   __device__ static __forceinline__ bool apply(In a, In b, uint32_t, Out& o) {
     uint64_t r = 0;
     const bool ok = int_op<OP, W>(a, b, r);
@@ -22,6 +54,16 @@ template <int W> struct ICmp {
   static constexpr bool kBinary = true;
   __device__ static __forceinline__ bool apply(In a, In b, uint32_t flags, Out& o) {
     o = cmpi<W>((int)((flags & DCF_FLAG_PRED_MASK) >> DCF_FLAG_PRED_SHIFT), a, b);
+    return true;
+  }
+};
+
+template <int W> struct ICarry {
+  using In = typename IntW<W>::T;
+  using Out = uint8_t;
+  static constexpr bool kBinary = true;
+  __device__ static __forceinline__ bool apply(In a, In b, uint32_t, Out& o) {
+    o = add_carry<W>(a, b);
     return true;
   }
 };
@@ -45,7 +87,13 @@ template <int W> static int int_binary_for(const EwLaunch& a) {
     case DCF_MAXUI: return launch_one<IOp<DCF_MAXUI, W>>(a);
     case DCF_MINSI: return launch_one<IOp<DCF_MINSI, W>>(a);
     case DCF_MINUI: return launch_one<IOp<DCF_MINUI, W>>(a);
+    case DCF_CEILDIVUI: return launch_one<IOp<DCF_CEILDIVUI, W>>(a);
+    case DCF_CEILDIVSI: return launch_one<IOp<DCF_CEILDIVSI, W>>(a);
+    case DCF_FLOORDIVSI: return launch_one<IOp<DCF_FLOORDIVSI, W>>(a);
+    case DCF_MULSI_HI: return launch_one<IOp<DCF_MULSI_HI, W>>(a);
+    case DCF_MULUI_HI: return launch_one<IOp<DCF_MULUI_HI, W>>(a);
     case DCF_CMPI: return launch_one<ICmp<W>>(a);
+    case DCF_ADDUI_CARRY: return launch_one<ICarry<W>>(a);
     default: return DCF_EUNSUPPORTED;
   }
 }

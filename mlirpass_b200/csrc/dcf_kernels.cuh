@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "dcf_elem.cuh"
 #include "dcf_launch.h"
 
@@ -112,6 +114,18 @@ __device__ __forceinline__ void load_chunk(const typename F::In* __restrict__ l,
   }
 }
 
+// Functors whose op never refuses and works lane-wise on 8- or 16-bit
+// elements may define `kWord` and `word(a, b)`: the op on four (or two)
+// elements packed in one 32-bit word (SIMD-within-a-register), so a
+// 16-byte chunk of i8 costs four operations instead of sixteen.
+template <class F, class = void> struct HasWord : std::false_type {};
+template <class F> struct HasWord<F, std::void_t<decltype(F::kWord)>> : std::bool_constant<F::kWord> {};
+
+template <class T> __device__ __forceinline__ uint32_t replicate32(T v) {
+  if constexpr (sizeof(T) == 1) return (uint32_t)(uint8_t)v * 0x01010101u;
+  else return (uint32_t)(uint16_t)v * 0x00010001u;
+}
+
 template <class F, int VEC>
 __device__ __forceinline__ void fold_chunk(typename F::Out* __restrict__ o, uint64_t c, uint64_t base,
                                            uint32_t flags, const typename F::In (&av)[VEC],
@@ -119,6 +133,20 @@ __device__ __forceinline__ void fold_chunk(typename F::Out* __restrict__ o, uint
                                            uint64_t& my_fail, bool& nonsplat) {
   using In = typename F::In;
   using Out = typename F::Out;
+  if constexpr (HasWord<F>::value && VEC * sizeof(In) == 16 && sizeof(Out) == sizeof(In)) {
+    const uint32_t* aw = (const uint32_t*)av;
+    const uint32_t* bw = (const uint32_t*)bv;
+    const uint32_t o0w = replicate32(o0);
+    uint4 r;
+    uint32_t* rw = (uint32_t*)&r;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      rw[k] = F::word(aw[k], bw[k]);
+      nonsplat |= rw[k] != o0w;
+    }
+    *(uint4*)(o + c * VEC) = r;
+    return;
+  }
   Out ov[VEC];
 #pragma unroll
   for (int k = 0; k < VEC; k++) {

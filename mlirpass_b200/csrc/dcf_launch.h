@@ -42,6 +42,28 @@ struct EwLaunch {
   int n_jobs = 0;
 };
 
+// Op classes (one place for the runtime, the batch entry points and the
+// kernel dispatch).
+inline bool op_float_binary(int op) { return (op >= DCF_ADDF && op <= DCF_REMF) || op == DCF_CMPF; }
+inline bool op_int_binary(int op) {
+  return (op >= DCF_ADDI && op <= DCF_MULUI_HI) || op == DCF_CMPI || op == DCF_ADDUI_CARRY;
+}
+inline bool op_binary(int op) { return op_float_binary(op) || op_int_binary(op); }
+// Binary ops whose result elements are i1 bytes.
+inline bool op_bool_result(int op) { return op == DCF_CMPI || op == DCF_CMPF || op == DCF_ADDUI_CARRY; }
+inline bool op_convert(int op) { return op >= DCF_EXTF && op <= DCF_TRUNCI; }
+// Whether a conversion op accepts the (from, to) element types.
+inline bool convert_types_ok(int op, bool from_float, bool from_int, bool to_float, bool to_int, int from, int to) {
+  switch (op) {
+    case DCF_EXTF: case DCF_TRUNCF: return from_float && to_float;
+    case DCF_SITOFP: case DCF_UITOFP: return from_int && to_float;
+    case DCF_FPTOSI: case DCF_FPTOUI: return from_float && to_int;
+    case DCF_NEGF: case DCF_FLUSH_DENORMALS: return from_float && from == to;
+    case DCF_EXTSI: case DCF_EXTUI: case DCF_TRUNCI: return from_int && to_int;
+    default: return false;
+  }
+}
+
 // Each returns DCF_OK, DCF_EUNSUPPORTED for an (op, type) pair it does not
 // handle, or DCF_ECUDA.
 int launch_float_binary(const EwLaunch& a);    // addf..minnumf, cmpf
@@ -55,6 +77,8 @@ int launch_permute(size_t elem_size, int rank, const int64_t* in_shape, const in
                    const void* in, void* out, cudaStream_t stream);
 int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t stream);
 int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st, cudaStream_t stream);
+int launch_select(size_t elem_size, const void* cond, int cond_splat, const void* t, int t_splat, const void* f,
+                  int f_splat, uint64_t n, void* out, dcf_status* st, cudaStream_t stream);
 int launch_splat_check(const void* in, size_t elem_size, uint64_t n, dcf_status* st, cudaStream_t stream);
 
 // Set the per-thread text dcf_last_error() returns; returns `code`.

@@ -81,23 +81,11 @@ bool prepare_smem(const void* kernel, int bytes) {
 }
 
 int launch_ew(const EwLaunch& a) {
-  switch (a.op) {
-    case DCF_ADDF: case DCF_SUBF: case DCF_MULF: case DCF_DIVF:
-    case DCF_MAXIMUMF: case DCF_MINIMUMF: case DCF_MAXNUMF: case DCF_MINNUMF:
-    case DCF_CMPF:
-      return launch_float_binary(a);
-    case DCF_ADDI: case DCF_SUBI: case DCF_MULI: case DCF_ANDI: case DCF_ORI: case DCF_XORI:
-    case DCF_SHLI: case DCF_SHRUI: case DCF_SHRSI: case DCF_DIVSI: case DCF_DIVUI:
-    case DCF_REMSI: case DCF_REMUI: case DCF_MAXSI: case DCF_MAXUI: case DCF_MINSI: case DCF_MINUI:
-    case DCF_CMPI:
-      return launch_int_binary(a);
-    case DCF_EXTF: case DCF_TRUNCF: case DCF_SITOFP: case DCF_UITOFP: case DCF_FPTOSI: case DCF_FPTOUI:
-      return launch_convert(a);
-    case DCF_RECIPROCAL:
-      return launch_reciprocal(a);
-    default:
-      return DCF_EUNSUPPORTED;
-  }
+  if (op_float_binary(a.op)) return launch_float_binary(a);
+  if (op_int_binary(a.op)) return launch_int_binary(a);
+  if (op_convert(a.op)) return launch_convert(a);
+  if (a.op == DCF_RECIPROCAL) return launch_reciprocal(a);
+  return DCF_EUNSUPPORTED;
 }
 
 // ------------------------------------------------------------ transpose
@@ -342,6 +330,92 @@ int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st
   note_launch();
   hex_decode_kernel<<<g, 256, 0, st>>>(in, nbytes, (uint8_t*)out, status, vec);
   return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+// --------------------------------------------------------------- select
+
+// Folder::select on three dense constants (src/patterns/arith/canonicalize.rs:869-875):
+// out[i] = cond[i] != 0 ? t[i] : f[i], a splat operand broadcast.  Chunks
+// of 16 elements: one 16-byte load of conditions and 16-byte loads of each
+// value operand, when every streamed pointer is 16-byte aligned (VEC).
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) select_kernel(const uint8_t* __restrict__ c, int cs, const T* __restrict__ t,
+                                                     int ts, const T* __restrict__ f, int fs, uint64_t n,
+                                                     T* __restrict__ o, dcf_status* st) {
+  constexpr int K = 16;
+  constexpr int TV = K * (int)sizeof(T) / 16;  // 16-byte vectors per operand chunk
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint8_t c0 = c[0];
+  const T t0 = t[0], f0 = f[0];
+  const T o0 = c0 ? t0 : f0;
+  bool nonsplat = false;
+  const uint64_t chunks = VEC ? n / K : 0;
+  for (uint64_t ch = tid; ch < chunks; ch += stride) {
+    uint8_t cv[K];
+    T tv[K], fv[K], ov[K];
+    if (cs) {
+#pragma unroll
+      for (int k = 0; k < K; k++) cv[k] = c0;
+    } else {
+      *(uint4*)cv = __ldg((const uint4*)(c + ch * K));
+    }
+    if (ts) {
+#pragma unroll
+      for (int k = 0; k < K; k++) tv[k] = t0;
+    } else {
+#pragma unroll
+      for (int j = 0; j < TV; j++) ((uint4*)tv)[j] = __ldg((const uint4*)(t + ch * K) + j);
+    }
+    if (fs) {
+#pragma unroll
+      for (int k = 0; k < K; k++) fv[k] = f0;
+    } else {
+#pragma unroll
+      for (int j = 0; j < TV; j++) ((uint4*)fv)[j] = __ldg((const uint4*)(f + ch * K) + j);
+    }
+#pragma unroll
+    for (int k = 0; k < K; k++) {
+      ov[k] = cv[k] ? tv[k] : fv[k];
+      nonsplat |= ov[k] != o0;
+    }
+#pragma unroll
+    for (int j = 0; j < TV; j++) ((uint4*)(o + ch * K))[j] = ((const uint4*)ov)[j];
+  }
+  for (uint64_t i = chunks * K + tid; i < n; i += stride) {
+    const T v = c[cs ? 0 : i] ? t[ts ? 0 : i] : f[fs ? 0 : i];
+    o[i] = v;
+    nonsplat |= v != o0;
+  }
+  report(st, ~0ull, nonsplat);
+}
+
+template <typename T>
+static int select_t(const void* c, int cs, const void* t, int ts, const void* f, int fs, uint64_t n, void* o,
+                    dcf_status* st, cudaStream_t s) {
+  auto al = [](const void* p, int splat) { return splat || ((uintptr_t)p & 15) == 0; };
+  const bool vec = al(c, cs) && al(t, ts) && al(f, fs) && al(o, 0);
+  const uint64_t need = ((vec ? n / 16 : n) + 255) / 256 + 1;
+  const int sms = sm_count();
+  const unsigned g = (unsigned)(need < (uint64_t)sms * 8 ? need : (uint64_t)sms * 8);
+  note_launch();
+  if (vec)
+    select_kernel<T, true><<<g, 256, 0, s>>>((const uint8_t*)c, cs, (const T*)t, ts, (const T*)f, fs, n, (T*)o, st);
+  else
+    select_kernel<T, false><<<g, 256, 0, s>>>((const uint8_t*)c, cs, (const T*)t, ts, (const T*)f, fs, n, (T*)o, st);
+  return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+int launch_select(size_t es, const void* c, int cs, const void* t, int ts, const void* f, int fs, uint64_t n, void* o,
+                  dcf_status* st, cudaStream_t s) {
+  if (n == 0) return DCF_OK;
+  switch (es) {
+    case 1: return select_t<uint8_t>(c, cs, t, ts, f, fs, n, o, st, s);
+    case 2: return select_t<uint16_t>(c, cs, t, ts, f, fs, n, o, st, s);
+    case 4: return select_t<uint32_t>(c, cs, t, ts, f, fs, n, o, st, s);
+    case 8: return select_t<uint64_t>(c, cs, t, ts, f, fs, n, o, st, s);
+    default: return DCF_EINVAL;
+  }
 }
 
 // ----------------------------------------------------------- splat test

@@ -64,12 +64,9 @@ int scratch_on(int dev, unsigned char** out) {
   return DCF_OK;
 }
 
-bool binary_op(uint32_t op) {
-  return (op >= DCF_ADDF && op <= DCF_MINNUMF) || (op >= DCF_ADDI && op <= DCF_MINUI) || op == DCF_CMPI ||
-         op == DCF_CMPF;
-}
+bool binary_op(uint32_t op) { return op_binary((int)op); }
 
-bool convert_op(uint32_t op) { return op >= DCF_EXTF && op <= DCF_FPTOUI; }
+bool convert_op(uint32_t op) { return op_convert((int)op); }
 
 }  // namespace
 
@@ -91,13 +88,11 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
     const bool bin = binary_op(j.op);
     bool ok;
     if (bin) {
-      const bool fop = (j.op >= DCF_ADDF && j.op <= DCF_MINNUMF) || j.op == DCF_CMPF;
-      ok = fop ? is_float(j.dtype) : is_int(j.dtype);
-      j.out_dtype = (j.op == DCF_CMPI || j.op == DCF_CMPF) ? DCF_I1 : j.dtype;
+      ok = op_float_binary((int)j.op) ? is_float(j.dtype) : is_int(j.dtype);
+      j.out_dtype = op_bool_result((int)j.op) ? DCF_I1 : j.dtype;
     } else if (convert_op(j.op)) {
-      if (j.op == DCF_EXTF || j.op == DCF_TRUNCF) ok = is_float(j.dtype) && is_float(j.out_dtype);
-      else if (j.op == DCF_SITOFP || j.op == DCF_UITOFP) ok = is_int(j.dtype) && is_float(j.out_dtype);
-      else ok = is_float(j.dtype) && is_int(j.out_dtype);
+      ok = convert_types_ok((int)j.op, is_float(j.dtype), is_int(j.dtype), is_float(j.out_dtype), is_int(j.out_dtype),
+                            (int)j.dtype, (int)j.out_dtype);
     } else if (j.op == DCF_RECIPROCAL) {
       ok = is_float(j.dtype);
       j.out_dtype = j.dtype;

@@ -102,8 +102,8 @@ struct Dev {
   void* h[2][3] = {{nullptr}};  // per slot: pinned staging
   dcf_status* st = nullptr;
   void* d0 = nullptr;           // 32 bytes: lhs element 0 at +0, rhs element 0 at +16
-  void* big[3] = {nullptr};     // whole-tensor buffers (transpose, batch)
-  size_t big_cap[3] = {0};
+  void* big[4] = {nullptr};     // whole-tensor buffers (transpose, select, batch)
+  size_t big_cap[4] = {0};
   void* hbig = nullptr;         // pinned whole-batch staging
   size_t hbig_cap = 0;
   // Elementwise pipeline: copy-in, compute and copy-out streams, with
@@ -172,7 +172,7 @@ void dev_free(Dev& d) {
   }
   for (cudaStream_t x : {d.sin, d.scomp, d.sout})
     if (x) cudaStreamDestroy(x);
-  for (int j = 0; j < 3; j++)
+  for (int j = 0; j < 4; j++)
     if (d.big[j]) cudaFree(d.big[j]);
   if (d.hbig) cudaFreeHost(d.hbig);
   if (d.st) cudaFree(d.st);
@@ -269,6 +269,13 @@ int h2d_full(Dev& d, void* dst, const void* src, size_t bytes, cudaStream_t s) {
     off += n;
     k ^= 1;
   }
+  // The staging buffers are free again only when their copies are done: a
+  // following h2d_full (another operand) refills them from the start.
+  for (int j = 0; j < 2; j++)
+    if (used[j]) {
+      int rc = wait_event(d.ev[j]);
+      if (rc) return rc;
+    }
   return DCF_OK;
 }
 
@@ -506,16 +513,13 @@ int run_elementwise(const EwJob& j, uint64_t n, dcf_result* res) {
   return DCF_OK;
 }
 
-bool binary_op(int op) {
-  return (op >= DCF_ADDF && op <= DCF_MINNUMF) || (op >= DCF_ADDI && op <= DCF_MINUI) || op == DCF_CMPI ||
-         op == DCF_CMPF;
-}
+bool binary_op(int op) { return op_binary(op); }
 
-bool convert_op(int op) { return op >= DCF_EXTF && op <= DCF_FPTOUI; }
+bool convert_op(int op) { return op_convert(op); }
 
 int check_binary(int op, int dtype) {
   if (!binary_op(op)) return set_err(DCF_EINVAL, "op %d is not a binary fold", op);
-  const bool fop = (op >= DCF_ADDF && op <= DCF_MINNUMF) || op == DCF_CMPF;
+  const bool fop = op_float_binary(op);
   if (fop && !is_float(dtype)) return set_err(DCF_EINVAL, "op %d needs a float dtype, got %d", op, dtype);
   if (!fop && !is_int(dtype)) return set_err(DCF_EINVAL, "op %d needs an integer dtype, got %d", op, dtype);
   return DCF_OK;
@@ -523,10 +527,7 @@ int check_binary(int op, int dtype) {
 
 int check_convert(int op, int from, int to) {
   if (!convert_op(op)) return set_err(DCF_EINVAL, "op %d is not a conversion fold", op);
-  bool ok = false;
-  if (op == DCF_EXTF || op == DCF_TRUNCF) ok = is_float(from) && is_float(to);
-  else if (op == DCF_SITOFP || op == DCF_UITOFP) ok = is_int(from) && is_float(to);
-  else ok = is_float(from) && is_int(to);
+  const bool ok = convert_types_ok(op, is_float(from), is_int(from), is_float(to), is_int(to), from, to);
   if (!ok) return set_err(DCF_EINVAL, "op %d cannot convert dtype %d to %d", op, from, to);
   return DCF_OK;
 }
@@ -571,7 +572,7 @@ int dcf_binary(dcf_op op, dcf_dtype dtype, const void* lhs, int lhs_splat, const
   if (rc) return rc;
   if (n && (!lhs || !rhs || !out)) return set_err(DCF_EINVAL, "null buffer");
   const size_t es = dtype_size(dtype);
-  const bool cmp = op == DCF_CMPI || op == DCF_CMPF;
+  const bool cmp = op_bool_result(op);
   EwJob j{op, dtype, dtype, flags, lhs, lhs_splat, rhs, rhs_splat, true, out, es, cmp ? 1 : es};
   return run_elementwise(j, n, res);
 }
@@ -667,6 +668,47 @@ int dcf_transpose(size_t elem_size, int rank, const int64_t* in_shape, const int
   return DCF_OK;
 }
 
+int dcf_select(size_t elem_size, const void* cond, int cond_splat, const void* t, int t_splat, const void* f,
+               int f_splat, uint64_t n, void* out, dcf_result* res) {
+  if (res) {
+    memset(res, 0, sizeof *res);
+    res->first_fail_index = UINT64_MAX;
+  }
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
+    return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
+  int rc = ensure_init();
+  if (rc) return rc;
+  if (n == 0) {
+    if (res) res->folded = 1, res->is_splat = 1;
+    return DCF_OK;
+  }
+  if (!cond || !t || !f || !out) return set_err(DCF_EINVAL, "null buffer");
+  Dev& d = *g_devs[0];
+  std::lock_guard<std::mutex> g(d.mu);
+  CK(cudaSetDevice(d.id));
+  const size_t cb = cond_splat ? 1 : n, tb = (t_splat ? 1 : n) * elem_size, fb = (f_splat ? 1 : n) * elem_size;
+  const size_t ob = n * elem_size;
+  if ((rc = ensure_big(d, 0, cb)) || (rc = ensure_big(d, 1, tb)) || (rc = ensure_big(d, 2, fb)) ||
+      (rc = ensure_big(d, 3, ob)))
+    return rc;
+  cudaStream_t s = d.s[0];
+  if ((rc = h2d_full(d, d.big[0], cond, cb, s)) || (rc = h2d_full(d, d.big[1], t, tb, s)) ||
+      (rc = h2d_full(d, d.big[2], f, fb, s)))
+    return rc;
+  CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), s));
+  if ((rc = launch_select(elem_size, d.big[0], cond_splat, d.big[1], t_splat, d.big[2], f_splat, n, d.big[3], d.st,
+                          s)))
+    return set_err(rc, "select launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if ((rc = d2h_full(d, out, d.big[3], ob, s))) return rc;
+  dcf_status st;
+  if ((rc = read_status(d, s, &st))) return rc;
+  if (res) {
+    res->folded = 1;
+    res->is_splat = st.splat_word != 0;
+  }
+  return DCF_OK;
+}
+
 int dcf_hex_encode(const void* in, uint64_t nbytes, char* out) {
   int rc = ensure_init();
   if (rc) return rc;
@@ -751,8 +793,7 @@ int dcf_batch(dcf_job* jobs, size_t n_jobs) {
     else rc = set_err(DCF_EINVAL, "job %zu: unknown op %u", i, j.op);
     if (rc) return rc;
     if (!bin && !convert_op(j.op)) j.out_dtype = j.dtype;
-    if (bin && (j.op == DCF_CMPI || j.op == DCF_CMPF)) j.out_dtype = DCF_I1;
-    if (bin && j.op != DCF_CMPI && j.op != DCF_CMPF) j.out_dtype = j.dtype;
+    if (bin) j.out_dtype = op_bool_result(j.op) ? DCF_I1 : j.dtype;
     if (j.n && (!j.lhs || !j.out || (bin && !j.rhs))) return set_err(DCF_EINVAL, "job %zu: null buffer", i);
   }
   std::vector<size_t> order;
@@ -927,7 +968,7 @@ int dcf_binary_async(dcf_op op, dcf_dtype dtype, const void* lhs, int lhs_splat,
   EwLaunch a;
   a.op = op;
   a.dtype = dtype;
-  a.out_dtype = (op == DCF_CMPI || op == DCF_CMPF) ? DCF_I1 : dtype;
+  a.out_dtype = op_bool_result(op) ? DCF_I1 : dtype;
   a.flags = flags;
   a.l = lhs;
   a.r = rhs;
@@ -983,6 +1024,19 @@ int dcf_reciprocal_async(dcf_dtype dtype, const void* in, int in_splat, uint64_t
   a.st = status;
   a.stream = (cudaStream_t)stream;
   return async_ew(a);
+}
+
+int dcf_select_async(size_t elem_size, const void* cond, int cond_splat, const void* t, int t_splat, const void* f,
+                     int f_splat, uint64_t n, void* out, dcf_status* status, void* stream) {
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
+    return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
+  if (n == 0) return DCF_OK;
+  if (!cond || !t || !f || !out || !status) return set_err(DCF_EINVAL, "null pointer");
+  int rc = select_device(out);
+  if (rc) return rc;
+  rc = launch_select(elem_size, cond, cond_splat, t, t_splat, f, f_splat, n, out, status, (cudaStream_t)stream);
+  if (rc) return set_err(rc, "select launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return DCF_OK;
 }
 
 int dcf_transpose2d_async(size_t elem_size, uint64_t rows, uint64_t cols, const void* in, void* out, void* stream) {

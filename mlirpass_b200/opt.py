@@ -21,7 +21,8 @@ BIN_PATH = os.path.join(_HERE, "dcfold-opt")
 class Stats(ctypes.Structure):
     _fields_ = [("parse_ms", ctypes.c_double), ("run_ms", ctypes.c_double), ("print_ms", ctypes.c_double),
                 ("folds", ctypes.c_ulonglong), ("refused", ctypes.c_ulonglong), ("h2d_bytes", ctypes.c_ulonglong),
-                ("d2h_bytes", ctypes.c_ulonglong), ("batches", ctypes.c_ulonglong)]
+                ("d2h_bytes", ctypes.c_ulonglong), ("batches", ctypes.c_ulonglong), ("upload_ms", ctypes.c_double),
+                ("fold_ms", ctypes.c_double), ("download_ms", ctypes.c_double)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}
@@ -40,7 +41,7 @@ def lib():
         if not os.path.exists(LIB_PATH):
             raise ImportError(f"{LIB_PATH} is missing: run `python -m mlirpass_b200.build` first")
         L = ctypes.CDLL(LIB_PATH)
-        L.dcf_opt_run.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+        L.dcf_opt_run.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
                                   ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t),
                                   ctypes.POINTER(Stats)]
         L.dcf_opt_run.restype = ctypes.c_int
@@ -50,20 +51,54 @@ def lib():
     return _lib
 
 
-def run(text: str | bytes, pipeline: str, n_gpus: int = 1, split_input_file: bool = False):
-    """Run `pipeline` over `text`; returns (printed module, stats dict)."""
+def _buffer(text):
+    """(address, size, keep-alive) of the text argument."""
+    if isinstance(text, str):
+        text = text.encode()
+    if isinstance(text, (bytes, bytearray)):
+        buf = ctypes.create_string_buffer(0) if not text else None
+        if buf is not None:
+            return ctypes.addressof(buf), 0, buf
+        if isinstance(text, bytes):
+            return ctypes.cast(ctypes.c_char_p(text), ctypes.c_void_p).value, len(text), text
+        arr = (ctypes.c_char * len(text)).from_buffer(text)
+        return ctypes.addressof(arr), len(text), arr
+    if hasattr(text, "data_ptr"):            # a torch uint8 tensor (for example in pinned memory)
+        return text.data_ptr(), text.numel() * text.element_size(), text
+    if hasattr(text, "ctypes"):              # a numpy array
+        return text.ctypes.data, text.nbytes, text
+    raise TypeError("text must be str, bytes, bytearray, a numpy array or a torch tensor")
+
+
+def pinned_text(text):
+    """Copy text into page-locked host memory (a torch uint8 tensor).  The
+    driver copies constants straight from pinned text to the GPU instead of
+    staging them through its own pinned slots."""
+    import numpy as np
+    import torch
     data = text.encode() if isinstance(text, str) else text
+    t = torch.empty(len(data), dtype=torch.uint8, pin_memory=True)
+    t.numpy()[:] = np.frombuffer(data, dtype=np.uint8)
+    return t
+
+
+def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as_bytes: bool = False):
+    """Run `pipeline` over `text` (str, bytes, or a uint8 buffer such as
+    pinned_text's); returns (printed module, stats dict).  The module is
+    str, or bytes with as_bytes=True."""
+    addr, size, keep = _buffer(text)
     out = ctypes.c_void_p()
     n = ctypes.c_size_t()
     st = Stats()
-    rc = lib().dcf_opt_run(data, len(data), pipeline.encode(), n_gpus, int(split_input_file), ctypes.byref(out),
+    rc = lib().dcf_opt_run(addr, size, pipeline.encode(), n_gpus, int(split_input_file), ctypes.byref(out),
                            ctypes.byref(n), ctypes.byref(st))
+    del keep
     if rc != 0:
         raise OptError(lib().dcf_opt_last_error().decode())
     try:
         # ctypes.string_at takes a C int size: copy through a sized array so
         # outputs above 2 GiB work.
-        s = bytes((ctypes.c_char * n.value).from_address(out.value)).decode() if n.value else ""
+        b = bytes((ctypes.c_char * n.value).from_address(out.value)) if n.value else b""
     finally:
         lib().dcf_opt_free(out)
-    return s, st.as_dict()
+    return (b if as_bytes else b.decode()), st.as_dict()

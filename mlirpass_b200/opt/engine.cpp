@@ -2,12 +2,17 @@
 #include "engine.h"
 
 #include <chrono>
+#include <condition_variable>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <stdexcept>
 #include <thread>
 #include <tuple>
+#include <unordered_map>
+#include <algorithm>
 
 namespace dco {
 
@@ -30,7 +35,7 @@ int hexval(char c) {
 
 // Host decode of a short hex literal (a splat element, a small list): not
 // worth a transfer and a launch.
-void decode_small(std::string_view hex, std::vector<uint8_t>& out) {
+void decode_small(std::string_view hex, Bytes& out) {
   out.resize(hex.size() / 2);
   for (size_t i = 0; i < out.size(); i++) {
     const int h = hexval(hex[2 * i]), l = hexval(hex[2 * i + 1]);
@@ -64,21 +69,100 @@ Pool& pool() {
   return *p;
 }
 
-// Run fn(0..n-1) on n threads and wait (n small: a copy split in parts).
+// A process-wide pool of host threads for the staging copies: one slot's
+// memcpy is split over several threads, and several engines (one per GPU)
+// submit at once.  Threads are started once, not per slot.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool* p = new CopyPool;  // never destroyed: workers may outlive static destructors
+    return *p;
+  }
+  int width() const { return (int)workers_.size() + 1; }
+  // Run fn(0..n-1); the caller takes part, and returns when all are done.
+  // fn is called only for parts taken before that, so it may live on the
+  // caller's stack; the batch record itself is shared with the workers.
+  template <class F>
+  void run(int n, F&& fn) {
+    if (n <= 1 || workers_.empty()) {
+      for (int i = 0; i < n; i++) fn(i);
+      return;
+    }
+    auto b = std::make_shared<Batch>();
+    b->fn = [&fn](int i) { fn(i); };
+    b->n = n;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      queue_.push_back(b);
+    }
+    cv_.notify_all();
+    work_on(*b);
+    std::unique_lock<std::mutex> g(mu_);
+    done_cv_.wait(g, [&] { return b->finished == b->n; });
+  }
+
+ private:
+  struct Batch {
+    std::function<void(int)> fn;
+    int n = 0;
+    int next = 0;      // guarded by mu_
+    int finished = 0;  // guarded by mu_
+  };
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  std::deque<std::shared_ptr<Batch>> queue_;
+  std::vector<std::thread> workers_;
+
+  CopyPool() {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const unsigned n = std::min(15u, hw > 1 ? hw - 1 : 0u);
+    for (unsigned i = 0; i < n; i++) workers_.emplace_back([this] { loop(); });
+    for (auto& t : workers_) t.detach();
+  }
+  // Take parts of b until none are left.
+  void work_on(Batch& b) {
+    for (;;) {
+      int i;
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        if (b.next >= b.n) return;
+        i = b.next++;
+      }
+      b.fn(i);
+      std::lock_guard<std::mutex> g(mu_);
+      if (++b.finished == b.n) done_cv_.notify_all();
+    }
+  }
+  void loop() {
+    for (;;) {
+      std::shared_ptr<Batch> b;
+      {
+        std::unique_lock<std::mutex> g(mu_);
+        cv_.wait(g, [&] {
+          while (!queue_.empty() && queue_.front()->next >= queue_.front()->n) queue_.pop_front();
+          return !queue_.empty();
+        });
+        b = queue_.front();
+      }
+      work_on(*b);
+    }
+  }
+};
+
+// Run fn(0..n-1) over the copy pool and wait.
 template <class F>
 void parallel(int n, F&& fn) {
-  if (n <= 1) {
-    fn(0);
-    return;
-  }
-  std::vector<std::thread> th;
-  for (int i = 1; i < n; i++) th.emplace_back([&, i] { fn(i); });
-  fn(0);
-  for (auto& t : th) t.join();
+  CopyPool::get().run(n, std::forward<F>(fn));
+}
+
+// Parts for a copy of `bytes`: about 2 MiB each, at most the pool's width.
+int parts_for(size_t bytes) {
+  const size_t p = bytes >> 21;
+  return (int)std::max<size_t>(1, std::min<size_t>(p, (size_t)CopyPool::get().width()));
 }
 
 void copy_parallel(void* dst, const void* src, size_t bytes) {
-  const int parts = bytes >= (8u << 20) ? 4 : 1;
+  const int parts = parts_for(bytes);
   parallel(parts, [&](int i) {
     const size_t a = bytes * (size_t)i / parts, b = bytes * (size_t)(i + 1) / parts;
     memcpy((char*)dst + a, (const char*)src + a, b - a);
@@ -201,6 +285,196 @@ void Engine::download(void* dst, const void* src, size_t bytes) {
   for (int j = 0; j < kSlots; j++) drain((k + j) % kSlots);
 }
 
+namespace {
+
+// Copy bytes [a, b) of a packed image between its pieces and `buf`, which
+// holds image byte `a` at offset 0.  Bytes between pieces are padding.
+void copy_span(const std::vector<ImagePiece>& pcs, size_t a, size_t b, char* buf, bool to_buf) {
+  auto it = std::upper_bound(pcs.begin(), pcs.end(), a,
+                             [](size_t x, const ImagePiece& p) { return x < p.off + p.len; });
+  for (; it != pcs.end() && it->off < b; ++it) {
+    const size_t lo = std::max(a, it->off), hi = std::min(b, it->off + it->len);
+    if (lo >= hi) continue;
+    char* h = (char*)it->host + (lo - it->off);
+    if (to_buf) memcpy(buf + (lo - a), h, hi - lo);
+    else memcpy(h, buf + (lo - a), hi - lo);
+  }
+}
+
+// Split [a, a+n) of the image over host threads (one for small spans).
+void copy_slot(const std::vector<ImagePiece>& pcs, size_t a, size_t n, char* buf, bool to_buf) {
+  const int parts = parts_for(n);
+  parallel(parts, [&](int i) {
+    const size_t x = n * (size_t)i / parts, y = n * (size_t)(i + 1) / parts;
+    copy_span(pcs, a + x, a + y, buf + x, to_buf);
+  });
+}
+
+size_t align16(size_t n) { return (n + 15) & ~(size_t)15; }
+
+}  // namespace
+
+// Host pieces -> pinned slots -> one contiguous device arena.
+void Engine::upload_image(const std::vector<ImagePiece>& pcs, size_t total, char* arena) {
+  ensure_pinned();
+  stats.h2d_bytes += total;
+  bool used[kSlots] = {false};
+  int k = 0;
+  for (size_t off = 0; off < total; off += kSlotBytes) {
+    const size_t n = std::min(kSlotBytes, total - off);
+    if (used[k]) ck(cudaEventSynchronize(slot_ev_[k]), "cudaEventSynchronize");
+    copy_slot(pcs, off, n, (char*)pinned_[k], true);
+    ck(cudaMemcpyAsync(arena + off, pinned_[k], n, cudaMemcpyHostToDevice, s_), "H2D");
+    ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
+    used[k] = true;
+    k = (k + 1) % kSlots;
+  }
+}
+
+// Device pieces -> pinned slots -> host pieces.  A slot is filled by one
+// copy per piece that overlaps it, then emptied by host threads while the
+// copy engine fills the next slots.
+void Engine::download_image(const std::vector<ImagePiece>& pcs, size_t total) {
+  ensure_pinned();
+  stats.d2h_bytes += total;
+  size_t pend_off[kSlots] = {0}, pend_n[kSlots] = {0};
+  auto drain = [&](int j) {
+    if (!pend_n[j]) return;
+    ck(cudaEventSynchronize(slot_ev_[j]), "cudaEventSynchronize");
+    copy_slot(pcs, pend_off[j], pend_n[j], (char*)pinned_[j], false);
+    pend_n[j] = 0;
+  };
+  size_t first = 0;  // first piece that may overlap the next slot
+  int k = 0;
+  for (size_t off = 0; off < total; off += kSlotBytes) {
+    const size_t n = std::min(kSlotBytes, total - off);
+    drain(k);
+    while (first < pcs.size() && pcs[first].off + pcs[first].len <= off) first++;
+    for (size_t i = first; i < pcs.size() && pcs[i].off < off + n; i++) {
+      const size_t lo = std::max(off, pcs[i].off), hi = std::min(off + n, pcs[i].off + pcs[i].len);
+      if (lo < hi)
+        ck(cudaMemcpyAsync((char*)pinned_[k] + (lo - off), (const char*)pcs[i].dev + (lo - pcs[i].off), hi - lo,
+                           cudaMemcpyDeviceToHost, s_),
+           "D2H");
+    }
+    ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
+    pend_off[k] = off;
+    pend_n[k] = n;
+    k = (k + 1) % kSlots;
+  }
+  for (int j = 0; j < kSlots; j++) drain((k + j) % kSlots);
+}
+
+void Engine::to_device_all(const std::vector<DenseValue*>& in) {
+  const auto t0 = std::chrono::steady_clock::now();
+  struct Timer {
+    double& acc;
+    std::chrono::steady_clock::time_point t;
+    ~Timer() { acc += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t).count(); }
+  } timer{stats.upload_ms, t0};
+  std::vector<DenseValue*> vs;
+  std::unordered_map<DenseValue*, size_t> index;
+  for (DenseValue* v : in) {
+    if (!v || (v->dev && v->dev->device == dev_) || v->bytes() == 0) continue;
+    if (index.emplace(v, vs.size()).second) vs.push_back(v);
+  }
+  if (vs.empty()) return;
+  if (vs.size() == 1) return to_device(*vs[0]);
+  set_device();
+  // Text and host bytes from pageable memory share one packed image that
+  // goes through the pinned slots; text inside page-locked input memory is
+  // copied straight from there into a second arena.  Peer-resident values
+  // are copied GPU to GPU.
+  std::vector<ImagePiece> staged, direct;
+  struct Loc {
+    DenseValue* v;
+    bool is_direct;
+    size_t off;
+  };
+  std::vector<Loc> text, raw;
+  size_t total = 0, total_direct = 0;
+  for (DenseValue* v : vs) {
+    if (v->poison) throw std::runtime_error("a poison value has no bytes");
+    if (!v->host.empty()) {
+      staged.push_back({(void*)v->host.data(), nullptr, v->bytes(), total});
+      raw.push_back({v, false, total});
+      total = align16(total + v->bytes());
+    } else if (!v->hex.empty() && in_pinned(v->hex.data(), v->hex.size())) {
+      direct.push_back({(void*)v->hex.data(), nullptr, v->hex.size(), total_direct});
+      text.push_back({v, true, total_direct});
+      total_direct = align16(total_direct + v->hex.size());
+    } else if (!v->hex.empty()) {
+      staged.push_back({(void*)v->hex.data(), nullptr, v->hex.size(), total});
+      text.push_back({v, false, total});
+      total = align16(total + v->hex.size());
+    } else if (!v->dev) {
+      throw std::runtime_error("constant has no bytes");
+    }
+  }
+  std::vector<std::shared_ptr<DeviceBuf>> bufs(vs.size());
+  for (size_t i = 0; i < vs.size(); i++) bufs[i] = std::make_shared<DeviceBuf>(dev_, vs[i]->bytes());
+  auto buf_of = [&](DenseValue* v) -> std::shared_ptr<DeviceBuf>& { return bufs[index.at(v)]; };
+  std::unique_ptr<DeviceBuf> arena, arena_direct;
+  if (total_direct) {
+    arena_direct = std::make_unique<DeviceBuf>(dev_, total_direct);
+    for (const ImagePiece& p : direct)
+      ck(cudaMemcpyAsync((char*)arena_direct->ptr + p.off, p.host, p.len, cudaMemcpyHostToDevice, s_), "H2D");
+    stats.h2d_bytes += total_direct;
+  }
+  if (total) {
+    arena = std::make_unique<DeviceBuf>(dev_, total);
+    upload_image(staged, total, (char*)arena->ptr);
+  }
+  auto at = [&](const Loc& l) {
+    return (const char*)(l.is_direct ? arena_direct->ptr : arena->ptr) + l.off;
+  };
+  if (!aux_) aux_ = std::make_unique<DeviceBuf>(dev_, sizeof(dcf_status));
+  dcf_status* st = (dcf_status*)aux_->ptr;
+  check(dcf_status_reset_async(st, s_), "status reset");
+  for (const Loc& l : text)
+    check(dcf_hex_decode_async(at(l), l.v->hex.size(), buf_of(l.v)->ptr, st, s_), "hex decode");
+  for (const Loc& l : raw)
+    ck(cudaMemcpyAsync(buf_of(l.v)->ptr, at(l), l.v->bytes(), cudaMemcpyDeviceToDevice, s_), "D2D");
+  for (DenseValue* v : vs)
+    if (v->host.empty() && v->hex.empty())
+      ck(cudaMemcpyPeerAsync(buf_of(v)->ptr, dev_, v->dev->ptr, v->dev->device, v->bytes(), s_), "peer copy");
+  dcf_status h;
+  ck(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s_), "D2H status");
+  sync();
+  if (h.first_fail != ~0ull) throw std::runtime_error("invalid hex digit in a dense literal");
+  for (size_t i = 0; i < vs.size(); i++) vs[i]->dev = bufs[i];
+}
+
+void Engine::to_host_all(const std::vector<DenseValue*>& in) {
+  const auto t0 = std::chrono::steady_clock::now();
+  std::vector<DenseValue*> vs;
+  std::unordered_map<DenseValue*, int> seen;
+  for (DenseValue* v : in) {
+    if (!v || !v->host.empty() || v->bytes() == 0 || !seen.emplace(v, 0).second) continue;
+    if (v->poison) throw std::runtime_error("a poison value has no bytes");
+    if (!v->hex.empty() && v->hex.size() <= kSmallHex) {
+      decode_small(v->hex, v->host);
+      continue;
+    }
+    vs.push_back(v);
+  }
+  if (vs.empty()) return;
+  std::vector<DenseValue*> off_device;
+  for (DenseValue* v : vs)
+    if (!v->dev || v->dev->device != dev_) off_device.push_back(v);
+  to_device_all(off_device);
+  set_device();
+  std::vector<ImagePiece> pcs;
+  size_t total = 0;
+  for (DenseValue* v : vs) {
+    if (v->host.data() == nullptr || v->host.size() != v->bytes()) v->host.resize(v->bytes());
+    pcs.push_back({v->host.data(), v->dev->ptr, v->bytes(), total});
+    total = align16(total + v->bytes());
+  }
+  download_image(pcs, total);
+  stats.download_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
 void Engine::set_device() {
   if (dev_ < 0) throw std::runtime_error("element work needs a GPU (the host-only engine folds nothing)");
   ck(cudaSetDevice(dev_), "cudaSetDevice");
@@ -263,7 +537,7 @@ void Engine::to_host(DenseValue& v) {
 
 uint64_t Engine::bits0_of(DenseValue& v) {
   if (v.host.empty() && !v.hex.empty()) {
-    std::vector<uint8_t> b;
+    Bytes b;
     decode_small(v.hex.substr(0, 2 * v.es), b);
     uint64_t x = 0;
     memcpy(&x, b.data(), v.es);
@@ -321,21 +595,27 @@ bool Engine::all_equal(DenseValue& v) {
 
 void Engine::execute(const std::vector<FoldRequest*>& reqs) {
   if (reqs.empty()) return;
-  const auto t0 = std::chrono::steady_clock::now();
   set_device();
   const size_t R = reqs.size();
   // Every streamed operand is made resident before the batch's statuses
   // are reset and its kernels are queued.
-  for (FoldRequest* q : reqs) {
-    if (q->lhs && !q->lhs->splat) to_device(*q->lhs);
-    if (q->rhs && !q->rhs->splat) to_device(*q->rhs);
+  {
+    std::vector<DenseValue*> ins;
+    for (FoldRequest* q : reqs) {
+      if (q->lhs && !q->lhs->splat) ins.push_back(q->lhs.get());
+      if (q->rhs && !q->rhs->splat) ins.push_back(q->rhs.get());
+      if (q->cond && !q->cond->splat) ins.push_back(q->cond.get());
+    }
+    to_device_all(ins);
   }
+  const auto t1 = std::chrono::steady_clock::now();
   dcf_status* st = statuses(R);
   ck(cudaMemsetAsync(st, 0xFF, R * sizeof(dcf_status), s_), "status reset");
 
   // Splat operands: one element each, packed 16-byte aligned and uploaded once.
   std::vector<uint8_t> scal;
   std::vector<std::pair<size_t, size_t>> spos(R, {SIZE_MAX, SIZE_MAX});
+  std::vector<size_t> cpos(R, SIZE_MAX);
   auto place = [&](DenseValue& v) {
     const size_t at = scal.size();
     scal.resize(at + 16, 0);
@@ -347,6 +627,7 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     FoldRequest& q = *reqs[i];
     if (q.lhs && q.lhs->splat) spos[i].first = place(*q.lhs);
     if (q.rhs && q.rhs->splat) spos[i].second = place(*q.rhs);
+    if (q.cond && q.cond->splat) cpos[i] = place(*q.cond);
   }
   std::unique_ptr<DeviceBuf> sdev;
   if (!scal.empty()) {
@@ -360,11 +641,12 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
   };
 
   std::vector<std::shared_ptr<DeviceBuf>> outs(R);
-  std::vector<const void*> ls(R, nullptr), rs(R, nullptr);
+  std::vector<const void*> ls(R, nullptr), rs(R, nullptr), cs(R, nullptr);
   for (size_t i = 0; i < R; i++) {
     FoldRequest& q = *reqs[i];
     ls[i] = q.lhs ? operand(*q.lhs, spos[i].first) : nullptr;
     rs[i] = q.rhs ? operand(*q.rhs, spos[i].second) : nullptr;
+    cs[i] = q.cond ? operand(*q.cond, cpos[i]) : nullptr;
     if (q.kind != FoldRequest::SPLAT_SCAN)
       outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * dcf_dtype_size((dcf_dtype)q.out_dtype));
   }
@@ -440,6 +722,11 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
       case FoldRequest::SPLAT_SCAN:
         check(dcf_splat_check_async(l, q.lhs->es, q.lhs->n, st + i, s_), "splat scan");
         break;
+      case FoldRequest::SELECT:
+        check(dcf_select_async(oes, cs[i], q.cond->splat, l, q.lhs->splat, r, q.rhs->splat, q.n, outs[i]->ptr, st + i,
+                               s_),
+              "select fold");
+        break;
     }
   }
   std::vector<dcf_status> hst(R);
@@ -491,7 +778,7 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     q.out = d;
   }
   stats.batches++;
-  stats.device_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  stats.device_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();
 }
 
 }  // namespace dco

@@ -38,10 +38,11 @@ class DeviceBuf {
 // One element-level fold.  The greedy driver fills the inputs; the engine
 // fills the outcome.
 struct FoldRequest {
-  enum Kind { BINARY, CONVERT, RECIPROCAL, PERMUTE, SPLAT_SCAN } kind = BINARY;
+  enum Kind { BINARY, CONVERT, RECIPROCAL, PERMUTE, SPLAT_SCAN, SELECT } kind = BINARY;
   int op = 0, dtype = 0, out_dtype = 0;
   uint32_t flags = 0;
   DenseP lhs, rhs;
+  DenseP cond;                          // SELECT: i1 conditions; lhs / rhs are the values
   uint64_t n = 0;                       // result elements
   std::vector<int64_t> shape, perms;    // PERMUTE
   TypeP out_ty;                         // attribute type of the result
@@ -52,9 +53,20 @@ struct FoldRequest {
   DenseP out;
 };
 
+// One constant's bytes inside a packed transfer image: many constants
+// travel through the pinned slots back to back, each at a 16-byte aligned
+// offset of the image.
+struct ImagePiece {
+  void* host;         // source (upload) or destination (download)
+  const void* dev;    // device source of a download
+  size_t len, off;    // bytes, offset in the image
+};
+
 struct EngineStats {
   uint64_t h2d_bytes = 0, d2h_bytes = 0, requests = 0, batches = 0;
-  double device_ms = 0;  // sum of batch wall times
+  double device_ms = 0;    // sum of batch wall times
+  double upload_ms = 0;    // to_device_all: staging, copies, decode
+  double download_ms = 0;  // to_host_all
 };
 
 // device < 0 makes a host-only engine: parsing, printing and the folds that
@@ -73,6 +85,12 @@ class Engine {
   void to_device(DenseValue& v);
   // Make its bytes available on the host (downloading if needed).
   void to_host(DenseValue& v);
+  // The same for many constants with one synchronisation: their hex texts
+  // (or host bytes) are packed back to back through the pinned slots into
+  // one device arena and decoded there; results come back through the
+  // slots the same way.
+  void to_device_all(const std::vector<DenseValue*>& vs);
+  void to_host_all(const std::vector<DenseValue*>& vs);
   // Uppercase hex digits of all its bytes (encoded on the device when
   // the value is there).
   std::string hex_of(DenseValue& v);
@@ -81,6 +99,13 @@ class Engine {
   bool all_equal(DenseValue& v);
 
   EngineStats stats;
+
+  // Host memory the copy engine can read directly (page-locked input
+  // text): constants inside it skip the staging slots.
+  void set_pinned_source(const void* begin, size_t bytes) {
+    pinned_src_ = (const char*)begin;
+    pinned_len_ = bytes;
+  }
 
   // Host <-> device copies of `bytes` (synchronous).  Large copies from
   // pageable memory go through pinned staging slots, filled and emptied by
@@ -91,6 +116,11 @@ class Engine {
  private:
   int dev_;
   cudaStream_t s_ = nullptr;
+  const char* pinned_src_ = nullptr;
+  size_t pinned_len_ = 0;
+  bool in_pinned(const void* p, size_t n) const {
+    return pinned_src_ && (const char*)p >= pinned_src_ && (const char*)p + n <= pinned_src_ + pinned_len_;
+  }
   std::unique_ptr<DeviceBuf> status_;   // dcf_status slots of a batch
   size_t status_cap_ = 0;
   std::unique_ptr<DeviceBuf> aux_;      // status word of uploads and scans outside a batch
@@ -99,6 +129,8 @@ class Engine {
   void* pinned_[kSlots] = {nullptr};
   cudaEvent_t slot_ev_[kSlots] = {nullptr};
   void ensure_pinned();
+  void upload_image(const std::vector<ImagePiece>& pcs, size_t total, char* arena);
+  void download_image(const std::vector<ImagePiece>& pcs, size_t total);
   void run_batched(const std::vector<FoldRequest*>& reqs, const std::vector<const void*>& ls,
                    const std::vector<const void*>& rs, std::vector<std::shared_ptr<DeviceBuf>>& outs,
                    std::vector<dcf_status>& hst);

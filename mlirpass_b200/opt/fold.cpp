@@ -268,6 +268,32 @@ class ArithFolder {
       if (zero(1)) return Plan::of_value(v(0));
       return int_binary(o == "shli" ? DCF_SHLI : o == "shrui" ? DCF_SHRUI : DCF_SHRSI);
     }
+    if (o == "ceildivui" || o == "ceildivsi" || o == "floordivsi") {  // :287-317
+      if (one(1)) return Plan::of_value(v(0));
+      return int_binary(o == "ceildivui" ? DCF_CEILDIVUI : o == "ceildivsi" ? DCF_CEILDIVSI : DCF_FLOORDIVSI);
+    }
+    if (o == "remf") return binary(DCF_REMF, 0, nullptr);  // :387
+    if (o == "negf") {                                       // :327-333
+      if (Op* inner = def(0, "arith.negf")) return Plan::of_value(inner->operands[0]);
+      return float_unary(DCF_NEGF);
+    }
+    if (o == "flush_denormals") {                            // :376-385
+      if (Op* inner = def(0, "arith.flush_denormals")) return Plan::of_value(inner->results[0]);
+      return float_unary(DCF_FLUSH_DENORMALS);
+    }
+    if (o == "convertf") return float_convert(DCF_TRUNCF);  // :386
+    if (o == "extui" || o == "extsi") {                      // :388-398
+      if (Op* inner = def(0, name.c_str())) {
+        m_.set_operand(op_, 0, inner->operands[0]);
+        return Plan::of_value(res());
+      }
+      if (!element_type(ty())->is_int()) return Plan::failed();
+      return unary(o == "extsi" ? DCF_EXTSI : DCF_EXTUI, element_type(ty())->dtype);
+    }
+    if (o == "trunci") return trunci();
+    if (o == "index_cast" || o == "index_castui") return index_cast(o == "index_cast");
+    if (o == "bitcast") return bitcast();
+    if (o == "select") return select();
     return Plan::failed();
   }
 
@@ -505,6 +531,100 @@ class ArithFolder {
       }
     }
     return float_convert(DCF_TRUNCF);
+  }
+
+  Plan float_unary(int dop) {
+    if (!element_type(ty())->is_float()) return Plan::failed();
+    return unary(dop, element_type(ty())->dtype);
+  }
+
+  static int width_or(Value* x, int dflt) {
+    const TypeP e = element_type(x->ty);
+    return e->is_int() ? int_width(e->dtype) : dflt;
+  }
+
+  Plan trunci() {  // :685-706
+    const int res_w = width_or(res(), 0);
+    for (const char* ext : {"arith.extui", "arith.extsi"})
+      if (Op* e = def(0, ext)) {
+        Value* src = e->operands[0];
+        if (width_or(src, 0) > res_w) {
+          m_.set_operand(op_, 0, src);
+          return Plan::of_value(res());
+        }
+        if (element_type(src->ty)->text == element_type(ty())->text) return Plan::of_value(src);
+      }
+    if (Op* t = def(0, "arith.trunci")) {
+      m_.set_operand(op_, 0, t->operands[0]);
+      return Plan::of_value(res());
+    }
+    if (!res_w) return Plan::failed();
+    return unary(DCF_TRUNCI, element_type(ty())->dtype);
+  }
+
+  // index_cast / index_castui (:435-454); index is a 64-bit integer.
+  Plan index_cast(bool is_signed) {
+    const int w = width_or(res(), 64);
+    if (DenseP k = cst(0)) {
+      if (!k->ty->is_int()) return Plan::failed();
+      const int wi = int_width(k->dtype);
+      const int dop = w < wi ? DCF_TRUNCI : (is_signed ? DCF_EXTSI : DCF_EXTUI);
+      return unary(dop, element_type(ty())->dtype);
+    }
+    if (Op* inner = def(0, op_->name.c_str())) {
+      Value* x = inner->operands[0];
+      if (x->ty->text == ty()->text && width_or(inner->results[0], 64) >= width_or(x, 64)) return Plan::of_value(x);
+    }
+    return Plan::failed();
+  }
+
+  // bitcast (:764-789): the same bits under the result's element type, so
+  // no element work; the new constant shares the operand's bytes.
+  Plan bitcast() {
+    if (!c_.size() || !c_[0]) return Plan::failed();
+    DenseP a = c_[0];
+    if (a->poison) return ty()->shaped() ? Plan::failed() : Plan::of_attr(a);
+    if (!a->elements && ty()->shaped()) return Plan::failed();
+    const TypeP target = a->elements ? ty() : element_type(ty());
+    if (!target->dtype || dcf_dtype_size((dcf_dtype)target->dtype) != a->es) return Plan::failed();
+    auto d = std::make_shared<DenseValue>(*a);
+    d->ty = target;
+    d->dtype = target->dtype;
+    return Plan::of_attr(d);
+  }
+
+  Plan select() {  // :841-876
+    Value *c = v(0), *t = v(1), *f = v(2);
+    if (t == f) return Plan::of_value(t);
+    if (one(0)) return Plan::of_value(t);
+    if (zero(0)) return Plan::of_value(f);
+    if (poison(1)) return Plan::of_value(f);
+    if (poison(2)) return Plan::of_value(t);
+    if (!ty()->shaped() && ty()->dtype == DCF_I1 && one(1) && zero(2)) return Plan::of_value(c);
+    if (Op* cmp = c->def; cmp && !cmp->erased && cmp->name == "arith.cmpi") {
+      bool ok = false;
+      const std::string* pp = cmp->prop("predicate");
+      const int64_t p = pp ? parse_int_prop(*pp, &ok) : -1;
+      if (ok && (p == 0 || p == 1)) {
+        Value *cl = cmp->operands[0], *cr = cmp->operands[1];
+        if ((cl == t && cr == f) || (cr == t && cl == f)) return Plan::of_value(p == 1 ? t : f);
+      }
+    }
+    DenseP kc = cst(0), kl = cst(1), kr = cst(2);
+    if (!kc || !kl || !kr) return Plan::failed();
+    if (!(kc->elements && kl->elements && kr->elements)) return Plan::failed();
+    if (kl->es != kr->es || !kl->ty->dtype) return Plan::failed();
+    auto q = std::make_unique<FoldRequest>();
+    q->kind = FoldRequest::SELECT;
+    q->dtype = kl->dtype;
+    q->out_dtype = kl->dtype;
+    q->cond = kc;
+    q->lhs = kl;
+    q->rhs = kr;
+    q->n = (uint64_t)std::max<int64_t>(1, kl->ty->count());
+    q->out_ty = kl->ty;
+    q->out_elements = true;
+    return Plan::device(std::move(q));
   }
 
   Plan float_convert(int dop) {  // :727-742
@@ -1162,6 +1282,9 @@ void run_pipeline(Module& m, const std::string& pipeline_in, std::vector<Engine*
 }
 
 void fetch_results(Module& m, std::vector<Engine*>& engines) {
+  // Every device-resident constant comes back to the host: one packed
+  // download per GPU, the GPUs in parallel.
+  std::unordered_map<Engine*, std::vector<DenseValue*>> per;
   std::vector<Op*> stack{m.top};
   while (!stack.empty()) {
     Op* o = stack.back();
@@ -1170,12 +1293,28 @@ void fetch_results(Module& m, std::vector<Engine*>& engines) {
       Engine* e = engines[0];
       for (Engine* x : engines)
         if (x->device() == o->cst->dev->device) e = x;
-      e->to_host(*o->cst);
+      per[e].push_back(o->cst.get());
     }
     for (Region* r : o->regions)
       for (Block* b : r->blocks)
         for (Op* in : b->ops) stack.push_back(in);
   }
+  std::vector<std::thread> th;
+  std::vector<std::string> errs(per.size());
+  size_t i = 0;
+  for (auto& kv : per) {
+    th.emplace_back([&, i, e = kv.first, vs = &kv.second] {
+      try {
+        e->to_host_all(*vs);
+      } catch (const std::exception& ex) {
+        errs[i] = ex.what();
+      }
+    });
+    i++;
+  }
+  for (auto& t : th) t.join();
+  for (auto& e : errs)
+    if (!e.empty()) throw std::runtime_error(e);
 }
 
 }  // namespace dco

@@ -2,6 +2,10 @@
 // MLIR float / int literal codecs of dcfold-opt.
 #include "ir.h"
 
+#include <algorithm>
+#include <atomic>
+#include <thread>
+
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -401,7 +405,7 @@ void flatten_list(const std::string& s, std::vector<std::string>& out) {
 
 class Parser {
  public:
-  Parser(const std::string& s, Module& m) : s_(s), m_(m) {}
+  Parser(std::string_view s, Module& m) : s_(s), m_(m) {}
 
   Op* parse_top() {
     scopes_.emplace_back();
@@ -414,7 +418,8 @@ class Parser {
   }
 
  private:
-  const std::string& s_;
+  const std::string_view s_;
+  std::string sub(size_t a, size_t n = std::string_view::npos) const { return std::string(s_.substr(a, n)); }
   Module& m_;
   size_t p_ = 0;
   struct Scope {
@@ -458,7 +463,7 @@ class Parser {
   // A balanced span starting here, ending before a top-level char in `stops`.
   std::string span(const char* stops) {
     const auto r = span_pos(stops);
-    return trim(s_.substr(r.first, r.second - r.first));
+    return trim(sub(r.first, r.second - r.first));
   }
 
   // The same, as [start, end) offsets: nothing is copied, and string
@@ -505,7 +510,7 @@ class Parser {
     ws();
     const size_t start = p_;
     while (p_ < s_.size() && (isalnum((unsigned char)s_[p_]) || strchr("_$.-#%^", s_[p_]))) p_++;
-    return s_.substr(start, p_ - start);
+    return sub(start, p_ - start);
   }
 
   void close_scope() {
@@ -638,7 +643,7 @@ class Parser {
     if (!eat('"')) fail("expected an op name string", p_);
     const size_t q = s_.find('"', p_);
     if (q == std::string::npos) fail("unterminated op name", p_);
-    Op* op = m_.new_op(s_.substr(p_, q - p_));
+    Op* op = m_.new_op(sub(p_, q - p_));
     p_ = q + 1;
     expect('(');
     std::vector<std::string> operand_refs;
@@ -652,16 +657,16 @@ class Parser {
       p_++;
       span("]");
       expect(']');
-      op->successors = s_.substr(a, p_ - a);
+      op->successors = sub(a, p_ - a);
     }
     if (eat("<{")) {
       while (!peek('}')) {
         const auto r = span_pos(",}");
         const size_t eq = s_.find('=', r.first);
         if (eq == std::string::npos || eq >= r.second) {
-          op->props.emplace_back(trim(s_.substr(r.first, r.second - r.first)), "");
+          op->props.emplace_back(trim(sub(r.first, r.second - r.first)), "");
         } else {
-          std::string key = trim(s_.substr(r.first, eq - r.first));
+          std::string key = trim(sub(r.first, eq - r.first));
           size_t va = eq + 1;
           while (va < r.second && isspace((unsigned char)s_[va])) va++;
           if (r.second - va > kBigProp) {
@@ -669,7 +674,7 @@ class Parser {
             op->big_value = std::string_view(s_.data() + va, r.second - va);
             op->props.emplace_back(std::move(key), "");
           } else {
-            op->props.emplace_back(std::move(key), s_.substr(va, r.second - va));
+            op->props.emplace_back(std::move(key), sub(va, r.second - va));
           }
         }
         if (!eat(',')) break;
@@ -693,7 +698,7 @@ class Parser {
       p_++;
       span("}");
       expect('}');
-      op->attrs = s_.substr(a, p_ - a);
+      op->attrs = sub(a, p_ - a);
     }
     expect(':');
     std::string fnty = span("\n");
@@ -765,13 +770,14 @@ class Parser {
     const std::string* text = op->prop(key);
     if (!text) return;
     const std::string_view full = (op->big_key == key) ? op->big_value : std::string_view(*text);
-    // Big literals: only the ends are examined here; the hex body is
-    // decoded (on the GPU) when the constant is first used.
-    if (full.size() > kBigProp) {
+    // Big hex literals: only the ends are examined here; the hex body is
+    // decoded (on the GPU) when the constant is first used.  Big literal
+    // lists (i1 constants, which print as lists) are parsed below.
+    const bool big_hex = full.size() > kBigProp && full.substr(0, 9) == "dense<\"0x";
+    if (big_hex) {
       const size_t colon = full.rfind(" : ");
       const size_t q0 = full.find("\"0x"), q1 = full.rfind('"');
-      if (colon == std::string_view::npos || q0 == std::string_view::npos || q1 <= q0 || full.substr(0, 6) != "dense<")
-        return;
+      if (colon == std::string_view::npos || q0 == std::string_view::npos || q1 <= q0) return;
       TypeP ty = type_of(std::string(full.substr(colon + 3)));
       if (!ty->dtype || !ty->static_shape() || ty->dtype == DCF_I1) return;
       auto d = std::make_shared<DenseValue>();
@@ -787,7 +793,7 @@ class Parser {
       op->cst_text = true;
       return;
     }
-    std::string lit = *text, ty_text;
+    std::string lit(full), ty_text;
     // split "literal : type" at the last top-level " : "
     {
       auto parts = split_top(lit, ':');
@@ -814,10 +820,11 @@ class Parser {
       std::string body = trim(lit.substr(6, lit.size() - 7));
       if (body.size() > 3 && body[0] == '"' && body[1] == '0' && body[2] == 'x') {
         if (ty->dtype == DCF_I1) return;  // bit-packed in MLIR's raw form
-        // Point into the source text: the attribute text lives in op->props.
-        const std::string* src = op->prop(key);
-        const size_t a = src->find("\"0x") + 3, b = src->find('"', a);
-        d->hex = std::string_view(src->data() + a, b - a);
+        // Point into the attribute text (op->props, or the input for a big
+        // literal).
+        const size_t a = full.find("\"0x") + 3, b = full.find('"', a);
+        if (a < 3 || b == std::string_view::npos) return;
+        d->hex = full.substr(a, b - a);
         const uint64_t bytes = d->hex.size() / 2;
         if (bytes == d->es) {
           d->splat = true;
@@ -862,7 +869,7 @@ class Parser {
 
 }  // namespace
 
-std::unique_ptr<Module> parse_module(const std::string& text) {
+std::unique_ptr<Module> parse_module(std::string_view text) {
   auto m = std::make_unique<Module>();
   Parser p(text, *m);
   m->top = p.parse_top();
@@ -906,18 +913,20 @@ class Printer {
         first = false;
         out += kv.first;
         if (o->cst && !o->cst_text && kv.first == key) {
-          out += " = " + value_text(*o->cst);
+          out += " = ";
+          put_value(*o->cst);
           wrote_value = true;
         } else if (kv.first == o->big_key && !o->big_value.empty()) {
           out += " = ";
-          out.append(o->big_value.data(), o->big_value.size());
+          defer(Fill::RAW, o->big_value.data(), o->big_value.size());
         } else if (!kv.second.empty()) {
           out += " = " + kv.second;
         }
       }
       if (o->cst && !o->cst_text && !wrote_value && !o->cst->poison) {
         if (!first) out += ", ";
-        out += std::string(key) + " = " + value_text(*o->cst);
+        out += std::string(key) + " = ";
+        put_value(*o->cst);
       }
       out += "}>";
     }
@@ -954,9 +963,18 @@ class Printer {
     out += "\n";
   }
 
+  // A large literal body is not copied into the skeleton: its place is
+  // recorded, and the final text is assembled from the skeleton and the
+  // bodies by several threads (PrintedModule::write_to).
+  using Fill = PrintedModule::Fill;
+  std::vector<Fill> fills;
+  static constexpr size_t kDeferBytes = 32768;
+
  private:
   const PrintHooks& h_;
   std::unordered_map<Value*, std::string> names_;
+
+  void defer(Fill::Kind k, const void* src, size_t nchars) { fills.push_back({k, src, nchars, out.size()}); }
   int next_ = 0, arg_ = 0;
 
   std::string name_of(Value* v) {
@@ -987,6 +1005,18 @@ class Printer {
     }
     out.append(indent, ' ');
     out += "}";
+  }
+
+  void put_value(DenseValue& v) {
+    const bool large = v.n > 100 && v.dtype != DCF_I1 && !v.splat && v.elements;
+    if (large && (!v.host.empty() || !v.hex.empty()) && v.bytes() >= kDeferBytes) {
+      out += "dense<\"0x";
+      if (!v.host.empty()) defer(Fill::HEX, v.host.data(), 2 * v.bytes());
+      else defer(Fill::UPPER, v.hex.data(), v.hex.size());
+      out += "\"> : " + v.ty->text;
+      return;
+    }
+    out += value_text(v);
   }
 
   std::string value_text(DenseValue& v) {
@@ -1045,11 +1075,107 @@ static size_t estimate(const Op* o) {
   return n;
 }
 
-std::string print_module(Module& m, const PrintHooks& hooks) {
+PrintedModule print_module_parts(Module& m, const PrintHooks& hooks) {
   Printer p(hooks);
   p.out.reserve(estimate(m.top));
   p.op(m.top, 0);
-  return std::move(p.out);
+  PrintedModule r;
+  r.skeleton = std::move(p.out);
+  r.fills = std::move(p.fills);
+  r.size_ = r.skeleton.size();
+  for (const auto& f : r.fills) r.size_ += f.nchars;
+  return r;
 }
+
+namespace {
+
+struct HexTable {
+  uint16_t pair[256];
+  HexTable() {
+    static const char d[] = "0123456789ABCDEF";
+    for (int b = 0; b < 256; b++) {
+      const char c[2] = {d[b >> 4], d[b & 15]};
+      memcpy(&pair[b], c, 2);
+    }
+  }
+};
+
+// Characters [c0, c1) of a body, written at dst.
+void fill_part(const PrintedModule::Fill& f, size_t c0, size_t c1, char* dst) {
+  switch (f.kind) {
+    case PrintedModule::Fill::RAW:
+      memcpy(dst, (const char*)f.src + c0, c1 - c0);
+      break;
+    case PrintedModule::Fill::UPPER: {
+      const char* s = (const char*)f.src + c0;
+      for (size_t i = 0; i < c1 - c0; i++) {
+        const char c = s[i];
+        dst[i] = (c >= 'a' && c <= 'f') ? (char)(c - 32) : c;
+      }
+      break;
+    }
+    case PrintedModule::Fill::HEX: {
+      static const HexTable t;
+      const uint8_t* b = (const uint8_t*)f.src + c0 / 2;  // c0, c1 even
+      const size_t n = (c1 - c0) / 2;
+      for (size_t i = 0; i < n; i++) memcpy(dst + 2 * i, &t.pair[b[i]], 2);
+      break;
+    }
+  }
+}
+
+}  // namespace
+
+void PrintedModule::write_to(char* dst) const {
+  // Tasks: skeleton spans and body chunks of at most kChunk characters,
+  // each with its output position; threads take them in order.
+  constexpr size_t kChunk = 4u << 20;
+  struct Task {
+    const Fill* f;  // null: skeleton span
+    size_t a, b;    // skeleton or body character range
+    size_t out;
+  };
+  std::vector<Task> tasks;
+  size_t pos = 0, sk = 0;
+  auto span = [&](size_t a, size_t b) {
+    for (size_t x = a; x < b; x += kChunk) {
+      const size_t y = std::min(b, x + kChunk);
+      tasks.push_back({nullptr, x, y, pos});
+      pos += y - x;
+    }
+  };
+  for (const Fill& f : fills) {
+    span(sk, f.at);
+    sk = f.at;
+    for (size_t x = 0; x < f.nchars; x += kChunk) {
+      const size_t y = std::min(f.nchars, x + kChunk);
+      tasks.push_back({&f, x, y, pos});
+      pos += y - x;
+    }
+  }
+  span(sk, skeleton.size());
+  std::atomic<size_t> next{0};
+  auto work = [&] {
+    for (size_t i; (i = next.fetch_add(1)) < tasks.size();) {
+      const Task& t = tasks[i];
+      if (t.f) fill_part(*t.f, t.a, t.b, dst + t.out);
+      else memcpy(dst + t.out, skeleton.data() + t.a, t.b - t.a);
+    }
+  };
+  const size_t hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t nth = std::min<size_t>({hw, 32, (size_ >> 22) + 1});
+  std::vector<std::thread> th;
+  for (size_t i = 1; i < nth; i++) th.emplace_back(work);
+  work();
+  for (auto& t : th) t.join();
+}
+
+std::string PrintedModule::str() const {
+  std::string s(size_, '\0');
+  write_to(&s[0]);
+  return s;
+}
+
+std::string print_module(Module& m, const PrintHooks& hooks) { return print_module_parts(m, hooks).str(); }
 
 }  // namespace dco

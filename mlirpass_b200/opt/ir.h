@@ -46,6 +46,29 @@ TypeP element_type(const TypeP& t);
 
 class DeviceBuf;  // engine.h
 
+// Host bytes of a constant.  resize() leaves new bytes uninitialised: they
+// are always overwritten by a download or a decode, and zero-filling a
+// multi-GiB result first would cost as much as the copy itself.
+template <class T>
+struct NoInit : std::allocator<T> {
+  template <class U>
+  struct rebind {
+    using other = NoInit<U>;
+  };
+  NoInit() = default;
+  template <class U>
+  NoInit(const NoInit<U>&) noexcept {}
+  template <class U>
+  void construct(U* p) noexcept {
+    ::new ((void*)p) U;
+  }
+  template <class U, class... A>
+  void construct(U* p, A&&... a) {
+    ::new ((void*)p) U(std::forward<A>(a)...);
+  }
+};
+using Bytes = std::vector<uint8_t, NoInit<uint8_t>>;
+
 // The value of a constant attribute: the reference's `Const` (values, type,
 // `elements` flag), stored as raw element bytes.  The bytes live on the
 // host, on a GPU, or (straight after parsing) as the hex text of a
@@ -58,7 +81,7 @@ struct DenseValue {
   int dtype = 0;
   size_t es = 0;             // element bytes
   uint64_t n = 0;            // stored elements (1 when splat)
-  std::vector<uint8_t> host; // host bytes, empty when not on the host
+  Bytes host;                // host bytes, empty when not on the host
   std::string_view hex;      // "HEX…" digits (no 0x), when parsed from text
   std::shared_ptr<DeviceBuf> dev;  // device bytes
   int all_equal = -1;        // cached "every value equal" test: -1 unknown
@@ -148,7 +171,7 @@ class Module {
 
 // Parse a module in MLIR's generic form.  `text` must outlive the module
 // (hex literals are decoded from it lazily).  Throws std::runtime_error.
-std::unique_ptr<Module> parse_module(const std::string& text);
+std::unique_ptr<Module> parse_module(std::string_view text);
 
 // Print the module in generic form.  Device-resident constants are fetched
 // through `fetch` (which fills DenseValue::host or returns hex digits).
@@ -159,6 +182,25 @@ struct PrintHooks {
   uint64_t (*bits0_of)(DenseValue& v, void* ctx) = nullptr;
   void* ctx = nullptr;
 };
+// A printed module: the text without its large literal bodies, plus where
+// each body goes.  write_to() assembles the text with several host threads
+// (the hex encoding of host bytes included).  The module and the parsed
+// text must outlive it.
+struct PrintedModule {
+  struct Fill {
+    enum Kind { RAW, UPPER, HEX } kind;
+    const void* src;  // characters (RAW, UPPER) or bytes (HEX)
+    size_t nchars;    // characters it prints
+    size_t at;        // skeleton position it goes before
+  };
+  std::string skeleton;
+  std::vector<Fill> fills;
+  size_t size_ = 0;
+  size_t size() const { return size_; }
+  void write_to(char* dst) const;
+  std::string str() const;
+};
+PrintedModule print_module_parts(Module& m, const PrintHooks& hooks);
 std::string print_module(Module& m, const PrintHooks& hooks);
 
 // Float literal helpers (MLIR syntax).

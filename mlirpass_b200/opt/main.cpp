@@ -52,8 +52,22 @@ struct Engines {
 std::string hex_hook(dco::DenseValue& v, void* ctx) { return ((Engines*)ctx)->of(v)->hex_of(v); }
 uint64_t bits_hook(dco::DenseValue& v, void* ctx) { return ((Engines*)ctx)->of(v)->bits0_of(v); }
 
-std::vector<std::string> split_chunks(const std::string& text, bool split) {
-  std::vector<std::string> out;
+// Whether the copy engine can read `text` in place (page-locked memory).
+bool is_pinned(std::string_view text) {
+  if (text.empty()) return false;
+  for (const char* p : {text.data(), text.data() + text.size() - 1}) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeHost) return false;
+  }
+  return true;
+}
+
+std::vector<std::string_view> split_chunks(std::string_view text, bool split) {
+  std::vector<std::string_view> out;
   if (!split) {
     out.push_back(text);
     return out;
@@ -61,28 +75,39 @@ std::vector<std::string> split_chunks(const std::string& text, bool split) {
   size_t a = 0;
   for (;;) {
     const size_t b = text.find("// -----", a);
-    out.push_back(text.substr(a, b == std::string::npos ? std::string::npos : b - a));
-    if (b == std::string::npos) break;
+    out.push_back(text.substr(a, b == std::string_view::npos ? std::string_view::npos : b - a));
+    if (b == std::string_view::npos) break;
     const size_t nl = text.find('\n', b);
-    a = nl == std::string::npos ? text.size() : nl + 1;
+    a = nl == std::string_view::npos ? text.size() : nl + 1;
   }
   return out;
 }
 
-std::string run_all(const std::string& text, const std::string& pipeline, int n_gpus, bool split,
-                    dcf_opt_stats* st) {
+// The printed result, malloc'd (handed to the C API's caller as is).
+struct Output {
+  char* p = nullptr;
+  size_t n = 0;
+};
+
+Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, bool split, dcf_opt_stats* st) {
   Engines eng(n_gpus);
-  std::string result;
   dcf_opt_stats total{};
   const auto chunks = split_chunks(text, split);
+  // Modules stay alive until the text is assembled: the printed parts
+  // point into their constants.
+  std::vector<std::unique_ptr<dco::Module>> mods;
+  std::vector<dco::PrintedModule> parts;
   for (size_t i = 0; i < chunks.size(); i++) {
     auto t0 = Clock::now();
-    std::unique_ptr<dco::Module> m = dco::parse_module(chunks[i]);
+    mods.push_back(dco::parse_module(chunks[i]));
+    dco::Module& m = *mods.back();
     total.parse_ms += ms_since(t0);
+    if (i == 0 && is_pinned(text))
+      for (auto* e : eng.list) e->set_pinned_source(text.data(), text.size());
     t0 = Clock::now();
     dco::PassStats ps;
-    dco::run_pipeline(*m, pipeline, eng.list, &ps);
-    dco::fetch_results(*m, eng.list);
+    dco::run_pipeline(m, pipeline, eng.list, &ps);
+    dco::fetch_results(m, eng.list);
     total.run_ms += ms_since(t0);
     total.folds += ps.folds;
     total.refused += ps.refused;
@@ -91,18 +116,36 @@ std::string run_all(const std::string& text, const std::string& pipeline, int n_
     hooks.hex_of = hex_hook;
     hooks.bits0_of = bits_hook;
     hooks.ctx = &eng;
-    if (i) result += "// -----\n";
-    if (chunks.size() == 1) result = dco::print_module(*m, hooks);
-    else result += dco::print_module(*m, hooks);
+    parts.push_back(dco::print_module_parts(m, hooks));
     total.print_ms += ms_since(t0);
   }
+  auto t0 = Clock::now();
+  static const char sep[] = "// -----\n";
+  Output out;
+  for (size_t i = 0; i < parts.size(); i++) out.n += parts[i].size() + (i ? sizeof sep - 1 : 0);
+  out.p = (char*)malloc(out.n + 1);
+  if (!out.p) throw std::runtime_error("out of memory for the printed module");
+  size_t at = 0;
+  for (size_t i = 0; i < parts.size(); i++) {
+    if (i) {
+      memcpy(out.p + at, sep, sizeof sep - 1);
+      at += sizeof sep - 1;
+    }
+    parts[i].write_to(out.p + at);
+    at += parts[i].size();
+  }
+  out.p[out.n] = 0;
+  total.print_ms += ms_since(t0);
   for (auto* e : eng.list) {
     total.h2d_bytes += e->stats.h2d_bytes;
     total.d2h_bytes += e->stats.d2h_bytes;
     total.batches += e->stats.batches;
+    total.upload_ms += e->stats.upload_ms;
+    total.download_ms += e->stats.download_ms;
+    total.fold_ms += e->stats.device_ms;
   }
   if (st) *st = total;
-  return result;
+  return out;
 }
 
 }  // namespace
@@ -114,16 +157,9 @@ extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, i
     return -1;
   }
   try {
-    std::string r = run_all(std::string(text, len), pipeline, n_gpus, split_input_file != 0, stats);
-    char* p = (char*)malloc(r.size() + 1);
-    if (!p) {
-      g_opt_err = "out of memory";
-      return -3;
-    }
-    memcpy(p, r.data(), r.size());
-    p[r.size()] = 0;
-    *out = p;
-    if (out_len) *out_len = r.size();
+    const Output r = run_all(std::string_view(text, len), pipeline, n_gpus, split_input_file != 0, stats);
+    *out = r.p;
+    if (out_len) *out_len = r.n;
     return 0;
   } catch (const std::exception& e) {
     g_opt_err = e.what();
@@ -182,12 +218,13 @@ int main(int argc, char** argv) {
   const std::string text = buf.str();
   dcf_opt_stats st{};
   try {
-    std::string r = run_all(text, pipeline, gpus, split, &st);
-    if (output == "-") fwrite(r.data(), 1, r.size(), stdout);
+    const Output r = run_all(text, pipeline, gpus, split, &st);
+    if (output == "-") fwrite(r.p, 1, r.n, stdout);
     else {
       std::ofstream f(output, std::ios::binary);
-      f.write(r.data(), (std::streamsize)r.size());
+      f.write(r.p, (std::streamsize)r.n);
     }
+    free(r.p);
   } catch (const std::exception& e) {
     fprintf(stderr, "dcfold-opt: %s\n", e.what());
     return 1;

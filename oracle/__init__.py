@@ -21,7 +21,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_build", "libdcforacle.so")
 
-from mlirpass_b200 import DTYPES, OPS, Fold, Result, as_storage, storage  # noqa: E402
+from mlirpass_b200 import BOOL_RESULT_OPS, DTYPES, OPS, Fold, Result, as_storage, storage  # noqa: E402
 
 _lib = None
 
@@ -38,6 +38,7 @@ def lib() -> ctypes.CDLL:
         L.dco_binary.argtypes = [i, i, vp, i, vp, i, u64, u32, vp, rp]
         L.dco_convert.argtypes = [i, i, i, vp, i, u64, u32, vp, rp]
         L.dco_reciprocal.argtypes = [i, vp, i, u64, u32, vp, rp]
+        L.dco_select.argtypes = [sz, vp, i, vp, i, vp, i, u64, vp, rp]
         L.dco_transpose.argtypes = [sz, i, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), vp, vp]
         L.dco_hex_encode.argtypes = [vp, u64, vp]
         L.dco_hex_decode.argtypes = [vp, u64, vp]
@@ -63,7 +64,7 @@ def binary(op, dtype, lhs, rhs, *, n=None, lhs_splat=False, rhs_splat=False, fla
     l, r = as_storage(lhs, dtype), as_storage(rhs, dtype)
     if n is None:
         n = 1 if (lhs_splat and rhs_splat) else max(len(l), len(r))
-    odt = "i1" if op in ("cmpi", "cmpf") else dtype
+    odt = "i1" if op in BOOL_RESULT_OPS else dtype
     if out is None:
         out = np.zeros(n, dtype=storage(odt))
     res = Result()
@@ -92,6 +93,19 @@ def reciprocal(dtype, x, *, n=None, splat=False, flags=0, out=None) -> Fold:
         out = np.zeros(n, dtype=storage(dtype))
     res = Result()
     _rc(lib().dco_reciprocal(DTYPES[dtype], _p(a), int(splat), n, flags, _p(out), ctypes.byref(res)))
+    return Fold(bool(res.folded), bool(res.is_splat), int(res.first_fail_index), out)
+
+
+def select(cond, t, f, *, n=None, cond_splat=False, t_splat=False, f_splat=False) -> Fold:
+    c = np.ascontiguousarray(cond, dtype=np.uint8).reshape(-1)
+    a = np.ascontiguousarray(t).reshape(-1)
+    b = np.ascontiguousarray(f).reshape(-1)
+    if n is None:
+        n = max(len(c), len(a), len(b))
+    out = np.zeros(n, dtype=a.dtype)
+    res = Result()
+    _rc(lib().dco_select(a.dtype.itemsize, _p(c), int(cond_splat), _p(a), int(t_splat), _p(b), int(f_splat), n,
+                         _p(out), ctypes.byref(res)))
     return Fold(bool(res.folded), bool(res.is_splat), int(res.first_fail_index), out)
 
 

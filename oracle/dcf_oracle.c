@@ -380,6 +380,51 @@ static int cmpi(int pred, int w, uint64_t a, uint64_t b) {
   }
 }
 
+/* ApInt's overflow-reporting signed steps at width w: the wrapped result
+ * and whether the exact result left [-2^(w-1), 2^(w-1)). */
+static uint64_t s_wrap(__int128 x, int w, int* ov) {
+  __int128 lo = -((__int128)1 << (w - 1)), hi = ((__int128)1 << (w - 1)) - 1;
+  if (x < lo || x > hi) *ov = 1;
+  return (uint64_t)x & wmask(w);
+}
+
+/* Folder::ceildivsi, src/patterns/arith/canonicalize.rs:557-595, step by
+ * step: ssub_ov / sdiv_ov / sadd_ov, any overflow refuses the element. */
+static int ceildivsi(int w, uint64_t ua, uint64_t ub, uint64_t* out) {
+  if (ub == 0) return 0;
+  if (ua == 0) { *out = 0; return 1; }
+  int ov = 0;
+  int64_t a = sext(ua, w), b = sext(ub, w);
+  /* ceil(a, b) for the two-positive case: (a - 1) / b + 1 */
+  #define CEIL_POS(x, y, res) do { \
+      int64_t s_ = sext(s_wrap((__int128)(x) - 1, w, &ov), w); \
+      int64_t q_; \
+      if ((y) == 0) { q_ = s_; ov = 1; } \
+      else { q_ = sext(s_wrap((__int128)s_ / (__int128)(y), w, &ov), w); } \
+      (res) = sext(s_wrap((__int128)q_ + 1, w, &ov), w); } while (0)
+  int64_t r;
+  if (a > 0 && b > 0) {
+    CEIL_POS(a, b, r);
+  } else if (a <= 0 && b <= 0) {
+    int64_t pa = sext(s_wrap(-(__int128)a, w, &ov), w);
+    int64_t pb = sext(s_wrap(-(__int128)b, w, &ov), w);
+    CEIL_POS(pa, pb, r);
+  } else if (a <= 0) {
+    int64_t pa = sext(s_wrap(-(__int128)a, w, &ov), w);
+    int64_t d = sext(s_wrap((__int128)pa / (__int128)b, w, &ov), w);
+    r = sext(s_wrap(-(__int128)d, w, &ov), w);
+  } else {
+    int64_t pb = sext(s_wrap(-(__int128)b, w, &ov), w);
+    if (pb == 0) return 0;
+    int64_t d = sext(s_wrap((__int128)a / (__int128)pb, w, &ov), w);
+    r = sext(s_wrap(-(__int128)d, w, &ov), w);
+  }
+  #undef CEIL_POS
+  if (ov) return 0;
+  *out = (uint64_t)r & wmask(w);
+  return 1;
+}
+
 /* Integer closures of ArithFolder::fold (wraparound ApInt arithmetic).
  * Returns 0 when the element refuses. */
 static int int_op(int op, int w, uint64_t a, uint64_t b, uint64_t* out) {
@@ -419,12 +464,53 @@ static int int_op(int op, int w, uint64_t a, uint64_t b, uint64_t* out) {
       if (ub == 0) return 0;
       *out = ua % ub;
       return 1;
+    case DCF_CEILDIVUI: {                                      /* :287-298 */
+      if (ub == 0) return 0;
+      uint64_t q = ua / ub;
+      if (ua % ub == 0) { *out = q; return 1; }
+      if (q == m) return 0;                                    /* uadd_ov */
+      *out = q + 1;
+      return 1;
+    }
+    case DCF_CEILDIVSI:                                        /* :557-595 */
+      return ceildivsi(w, ua, ub, out);
+    case DCF_FLOORDIVSI: {                                     /* :306-317 */
+      if (ub == 0) return 0;
+      if (sa == smin && sb == -1) return 0;                    /* sdiv_ov */
+      int64_t q = sa / sb, r = sa % sb;
+      if (r != 0 && ((r < 0) != (sb < 0))) q -= 1;
+      *out = (uint64_t)q & m;
+      return 1;
+    }
+    case DCF_MULSI_HI: {                                       /* :939-944 */
+      __int128 p = (__int128)sa * (__int128)sb;
+      *out = (uint64_t)(p >> w) & m;
+      return 1;
+    }
+    case DCF_MULUI_HI: {
+      unsigned __int128 p = (unsigned __int128)ua * (unsigned __int128)ub;
+      *out = (uint64_t)(p >> w) & m;
+      return 1;
+    }
     case DCF_MAXSI: *out = (sa > sb) ? ua : ub; return 1;     /* :679-682 */
     case DCF_MAXUI: *out = (ua > ub) ? ua : ub; return 1;
     case DCF_MINSI: *out = (sa < sb) ? ua : ub; return 1;
     case DCF_MINUI: *out = (ua < ub) ? ua : ub; return 1;
     default: return 0;
   }
+}
+
+/* remf: `x % y` through ApFloat::binary (src/patterns/arith/canonicalize.rs:387),
+ * Rust's remainder of truncating division.  It is exact, so the double
+ * fmod of the exactly widened operands narrows back without rounding.
+ * NaN operands and invalid cases follow the same rule as ap_arith. */
+static uint64_t remf(fl_t f, uint64_t a, uint64_t b, uint32_t flags) {
+  if (f_isnan(f, a)) return f_quiet(f, a);
+  if (f_isnan(f, b)) return f_quiet(f, b);
+  if (f_isinf(f, a) || f_iszero(f, b)) return f_default_nan(f, flags);
+  if (f_isinf(f, b) || f_iszero(f, a)) return a;
+  double x = f_to_double(f, a), y = f_to_double(f, b);
+  return f_convert(F64L, f, double_bits(fmod(x, y)));
 }
 
 /* --------------------------------------------------------- array folds */
@@ -449,14 +535,14 @@ int dco_binary(int op, int dtype, const void* lhs, int lhs_splat,
   res_init(res);
   int ib = elem_bytes(dtype);
   if (!ib) return DCF_EINVAL;
-  int is_cmp = (op == DCF_CMPI || op == DCF_CMPF);
+  int is_cmp = (op == DCF_CMPI || op == DCF_CMPF || op == DCF_ADDUI_CARRY);
   int ob = is_cmp ? 1 : ib;
   int w = int_width(dtype);
   fl_t f;
   int isf = fl_of(dtype, &f);
   int pred = (int)((flags & DCF_FLAG_PRED_MASK) >> DCF_FLAG_PRED_SHIFT);
   int mode = (int)(flags & DCF_FLAG_ROUND_MASK);
-  int fop = op >= DCF_ADDF && op <= DCF_MINNUMF;
+  int fop = op >= DCF_ADDF && op <= DCF_REMF;
   if ((fop || op == DCF_CMPF) && !isf) return DCF_EINVAL;
   if (!fop && op != DCF_CMPF && !w) return DCF_EINVAL;
   for (uint64_t i = 0; i < n; i++) {
@@ -474,6 +560,10 @@ int dco_binary(int op, int dtype, const void* lhs, int lhs_splat,
       case DCF_MINNUMF: r = minmax(f, a, b, 0, 0); break;
       case DCF_CMPF: r = (uint64_t)cmpf(pred, f, a, b); break;
       case DCF_CMPI: r = (uint64_t)cmpi(pred, w, a, b); break;
+      case DCF_REMF: r = remf(f, a, b, flags); break;
+      case DCF_ADDUI_CARRY:                                    /* :887-891 */
+        r = (uint64_t)((((a & wmask(w)) + (b & wmask(w))) & wmask(w)) < (a & wmask(w)));
+        break;
       default: ok = int_op(op, w, a, b, &r); break;
     }
     if (!ok) {
@@ -587,6 +677,8 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
     case DCF_EXTF: case DCF_TRUNCF: if (!fromf || !tof) return DCF_EINVAL; break;
     case DCF_SITOFP: case DCF_UITOFP: if (!wf || !tof) return DCF_EINVAL; break;
     case DCF_FPTOSI: case DCF_FPTOUI: if (!fromf || !wt) return DCF_EINVAL; break;
+    case DCF_NEGF: case DCF_FLUSH_DENORMALS: if (!fromf || from != to) return DCF_EINVAL; break;
+    case DCF_EXTSI: case DCF_EXTUI: case DCF_TRUNCI: if (!wf || !wt) return DCF_EINVAL; break;
     default: return DCF_EINVAL;
   }
   for (uint64_t i = 0; i < n; i++) {
@@ -597,7 +689,16 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
       case DCF_SITOFP: r = int_to_float(wf, a, 1, to, tf); break;
       case DCF_UITOFP: r = int_to_float(wf, a, 0, to, tf); break;
       case DCF_FPTOSI: ok = float_to_int(ff, a, wt, 1, &r); break;
-      default: ok = float_to_int(ff, a, wt, 0, &r); break;
+      case DCF_FPTOUI: ok = float_to_int(ff, a, wt, 0, &r); break;
+      /* negf: ApFloat::neg, the sign flipped (:327-333) */
+      case DCF_NEGF: r = a ^ (1ull << (ff.E + ff.M)); break;
+      /* flush_denormal (:69-77) */
+      case DCF_FLUSH_DENORMALS:
+        r = (f_expf(ff, a) == 0 && f_mant(ff, a) != 0) ? ((uint64_t)f_sign(ff, a) << (ff.E + ff.M)) : a;
+        break;
+      /* ApInt sext / zext / trunc (:388-398, :685-706) */
+      case DCF_EXTSI: r = (uint64_t)sext(a, wf) & wmask(wt); break;
+      default: r = a & wmask(wf) & wmask(wt); break;
     }
     if (!ok) {
       if (res) res->first_fail_index = i;
@@ -606,6 +707,22 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
     store(out, i, ob, r);
   }
   res_finish(res, out, ob, n);
+  return 0;
+}
+
+/* Folder::select on three dense constants (src/patterns/arith/canonicalize.rs:869-875):
+ * out[i] = cond[i] != 0 ? t[i] : f[i]; a splat operand broadcasts. */
+int dco_select(size_t elem_size, const uint8_t* cond, int cond_splat, const void* t, int t_splat,
+               const void* f, int f_splat, uint64_t n, void* out, dcf_result* res) {
+  res_init(res);
+  int es = (int)elem_size;
+  if (es != 1 && es != 2 && es != 4 && es != 8) return DCF_EINVAL;
+  for (uint64_t i = 0; i < n; i++) {
+    int c = cond[cond_splat ? 0 : i] != 0;
+    uint64_t v = c ? load(t, t_splat ? 0 : i, es) : load(f, f_splat ? 0 : i, es);
+    store(out, i, es, v);
+  }
+  res_finish(res, out, es, n);
   return 0;
 }
 

@@ -35,6 +35,8 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
                 uint64_t n, uint32_t flags, void* out, dcf_result* res);
 int dco_reciprocal(int dtype, const void* in, int in_splat, uint64_t n,
                    uint32_t flags, void* out, dcf_result* res);
+int dco_select(size_t elem_size, const uint8_t* cond, int cond_splat, const void* t, int t_splat,
+               const void* f, int f_splat, uint64_t n, void* out, dcf_result* res);
 int dco_transpose(size_t elem_size, int rank, const int64_t* in_shape,
                   const int64_t* perms, const void* in, void* out);
 int dco_hex_encode(const void* in, uint64_t nbytes, char* out);

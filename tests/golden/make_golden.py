@@ -34,12 +34,14 @@ REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
 FIX = os.path.join(REF, "tests", "fixtures")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "fold_vectors.json")
 
-BINARY_F = {"addf", "subf", "mulf", "divf", "maximumf", "minimumf", "maxnumf", "minnumf"}
+BINARY_F = {"addf", "subf", "mulf", "divf", "maximumf", "minimumf", "maxnumf", "minnumf", "remf"}
 BINARY_I = {"addi", "subi", "muli", "andi", "ori", "xori", "shli", "shrui", "shrsi",
-            "divsi", "divui", "remsi", "remui", "maxsi", "maxui", "minsi", "minui"}
-CONVERT = {"extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui"}
+            "divsi", "divui", "remsi", "remui", "maxsi", "maxui", "minsi", "minui",
+            "ceildivui", "ceildivsi", "floordivsi"}
+CONVERT = {"extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "convertf", "negf", "flush_denormals",
+           "extsi", "extui", "trunci", "index_cast", "index_castui", "bitcast"}
 CMP = {"cmpi", "cmpf"}
-ARITH = BINARY_F | BINARY_I | CONVERT | CMP
+ARITH = BINARY_F | BINARY_I | CONVERT | CMP | {"select"}
 TOSA = {"reciprocal", "transpose"}
 
 ALLOWED_FLAGS = ("-split-input-file", "--split-input-file", "-allow-unregistered-dialect",
@@ -127,6 +129,14 @@ def shortcut(op: str, ops, consts, props) -> str | None:
                 return "value0"
             if op.endswith("numf") and f_is(r, dt, "nan"):
                 return "value0"
+    if op == "select":
+        t_same = ops[1].result == ops[2].result
+        c = scalar_of(consts[0])
+        if t_same:
+            return "value1"
+        if c is not None:
+            return "value1" if c != 0 else "value2"
+        return None
     if op in BINARY_I or op == "cmpi":
         zero = r is not None and r == 0
         one = r is not None and r == 1
@@ -141,7 +151,7 @@ def shortcut(op: str, ops, consts, props) -> str | None:
             return "value1"
         if op == "muli" and one:
             return "value0"
-        if op in ("divsi", "divui") and one:
+        if op in ("divsi", "divui", "ceildivui", "ceildivsi", "floordivsi") and one:
             return "value0"
         if op in ("remsi", "remui") and one:
             return "zero"

@@ -111,15 +111,13 @@ def parse_type(s: str) -> Ty | None:
     if not m:
         return None
     kind, body = m.groups()
-    parts = body.split("x")
-    elem = parts[-1]
+    # leading "NxMx..." dims, then the element type (which may contain an
+    # "x" itself, as index does)
+    dm = re.match(r"^((?:\d+x)*)(.+)$", body)
+    elem = dm.group(2)
     if elem not in FLOATS and elem not in INTS:
-        return None
-    dims = []
-    for p in parts[:-1]:
-        if not p.isdigit():
-            return None        # dynamic or scalable dims
-        dims.append(int(p))
+        return None            # dynamic or scalable dims, or another element type
+    dims = [int(p) for p in dm.group(1).split("x") if p]
     return Ty(elem, dims, kind)
 
 

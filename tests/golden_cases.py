@@ -22,6 +22,8 @@ STORAGE = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
 SIZE = {"i1": 1, "i8": 1, "i16": 2, "i32": 4, "i64": 8, "index": 8, "f16": 2, "bf16": 2, "f32": 4, "f64": 8,
         "f8E5M2": 1, "f8E4M3": 1, "f8E3M4": 1}
 CANON = {"index": "i64"}
+UNARY = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "convertf", "negf", "flush_denormals", "extsi",
+         "extui", "trunci", "index_cast", "index_castui")
 
 
 def load_cases():
@@ -66,13 +68,35 @@ def run_case(c, eng):
         else:
             raise ValueError(op)
         return ("folded", (True, [int(x) for x in f.out[:1]])) if f.folded else ("not_folded", None)
-    if op in ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui"):
+    if op == "bitcast":
+        # ApInt::from_bits / ApFloat::from_bits of the same bits
+        # (src/patterns/arith/canonicalize.rs:764-789): no element work.
+        a, dt = _arr(ops[0])
+        return "folded", (ops[0]["splat"], [int(x) for x in a])
+    if op in UNARY:
         a, dt = _arr(ops[0])
         n = 1 if ops[0]["splat"] else len(a)
-        f = eng.convert(op, dt, rdt, a, n=n, splat=ops[0]["splat"])
+        eop = op
+        if op == "convertf":
+            eop = "truncf"   # the same float_convert closure (:386)
+        elif op in ("index_cast", "index_castui"):
+            # sext / zext to the wider width, then trunc (:435-454)
+            wi, wo = SIZE[dt], SIZE[rdt]
+            eop = "trunci" if wo < wi else ("extsi" if op == "index_cast" else "extui")
+        f = eng.convert(eop, dt, rdt, a, n=n, splat=ops[0]["splat"])
         if not f.folded:
             return "not_folded", None
         return "folded", (ops[0]["splat"], [int(x) for x in f.out[:n]])
+    if op == "select":
+        (cnd, _), (t, dt), (fv, _) = _arr(ops[0]), _arr(ops[1]), _arr(ops[2])
+        if not (ops[0]["elements"] and ops[1]["elements"] and ops[2]["elements"]):
+            return "not_folded", None
+        n = 1
+        for d in ops[1]["shape"] or []:
+            n *= d
+        f = eng.select(cnd, t, fv, n=n, cond_splat=ops[0]["splat"], t_splat=ops[1]["splat"],
+                       f_splat=ops[2]["splat"])
+        return "folded", (False, [int(x) for x in f.out[:n]])
     # binary
     (a, dt), (b, dt2) = _arr(ops[0]), _arr(ops[1])
     if dt != dt2 or ops[0]["elements"] != ops[1]["elements"] or ops[0]["shape"] != ops[1]["shape"]:

@@ -41,6 +41,8 @@ def literal(o):
         return one(bits[0]) if dt == "i1" else f"{one(bits[0])} : {ty_text(o)}"
     if o["splat"]:
         return f"dense<{one(bits[0])}> : {ty_text(o)}"
+    if dt == "i1":   # i1 constants are written as lists (MLIR's raw i1 form is bit-packed)
+        return f"dense<[{', '.join(one(b) for b in bits)}]> : {ty_text(o)}"
     raw = np.array(bits, dtype=STORAGE[SIZE[dt]]).tobytes().hex().upper()
     return f'dense<"0x{raw}"> : {ty_text(o)}'
 
@@ -189,3 +191,76 @@ def test_canonicalize_alone_leaves_non_splat_tosa_folds():
     fs = parse_funcs(out)
     assert any(o.name == "tosa.reciprocal" for o in fs["f0"].ops)
     assert any(o.name == "tosa.transpose" for o in fs["weights"].ops)
+
+
+def _gpus():
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_config5_sharded_over_gpus_prints_the_same(n):
+    # Functions are placed on the GPUs by constant bytes; the printed module
+    # must not depend on how many GPUs folded it.
+    if _gpus() < n:
+        pytest.skip(f"needs {n} GPUs")
+    text = mlir_gen.config5_text(64, 64, 512)
+    one, s1 = opt.run(text, mlir_gen.LAYERWISE, n_gpus=1)
+    many, sn = opt.run(text, mlir_gen.LAYERWISE, n_gpus=n)
+    assert many == one
+    assert sn["folds"] == s1["folds"] == 3 * 64 + 1
+
+
+def _hex(a):
+    return a.tobytes().hex().upper()
+
+
+def test_more_arith_folds_through_canonicalize(oracle):
+    # The remaining elementwise folds at a size where every one of them is
+    # a device fold, through the whole driver, against the oracle.
+    from test_gpu_parity import rbits
+    n = 1 << 18
+    T32, Ti1, Ti8, Ti64 = f"tensor<{n}xi32>", f"tensor<{n}xi1>", f"tensor<{n}xi8>", f"tensor<{n}xindex>"
+    F = f"tensor<{n}xf32>"
+    x, y = rbits("i32", n, 1), rbits("i32", n, 2)
+    y = np.where(y == 0, np.uint32(5), y)
+    y = np.where((x == 0x80000000) | (y == 0x80000000), np.uint32(7), y)  # keep ceildivsi folding
+    x = np.where(x == 0x80000000, np.uint32(9), x)
+    fa, fb = rbits("f32", n, 3), rbits("f32", n, 4)
+    c = rbits("i1", n, 5)
+    lines = [
+        f'    %x = "arith.constant"() <{{value = dense<"0x{_hex(x)}"> : {T32}}}> : () -> {T32}',
+        f'    %y = "arith.constant"() <{{value = dense<"0x{_hex(y)}"> : {T32}}}> : () -> {T32}',
+        f'    %fa = "arith.constant"() <{{value = dense<"0x{_hex(fa)}"> : {F}}}> : () -> {F}',
+        f'    %fb = "arith.constant"() <{{value = dense<"0x{_hex(fb)}"> : {F}}}> : () -> {F}',
+        f'    %c = "arith.constant"() <{{value = dense<[{", ".join("true" if v else "false" for v in c)}]> : {Ti1}}}> '
+        f': () -> {Ti1}',
+        f'    %0 = "arith.floordivsi"(%x, %y) : ({T32}, {T32}) -> {T32}',
+        f'    %1 = "arith.ceildivsi"(%x, %y) : ({T32}, {T32}) -> {T32}',
+        f'    %2 = "arith.ceildivui"(%x, %y) : ({T32}, {T32}) -> {T32}',
+        f'    %3 = "arith.remf"(%fa, %fb) <{{fastmath = #arith.fastmath<none>}}> : ({F}, {F}) -> {F}',
+        f'    %4 = "arith.negf"(%fa) <{{fastmath = #arith.fastmath<none>}}> : ({F}) -> {F}',
+        f'    %5 = "arith.flush_denormals"(%fb) <{{fastmath = #arith.fastmath<none>}}> : ({F}) -> {F}',
+        f'    %6 = "arith.trunci"(%x) <{{overflowFlags = #arith.overflow<none>}}> : ({T32}) -> {Ti8}',
+        f'    %7 = "arith.extsi"(%6) : ({Ti8}) -> {T32}',
+        f'    %8 = "arith.index_cast"(%y) : ({T32}) -> {Ti64}',
+        f'    %9 = "arith.bitcast"(%fa) : ({F}) -> {T32}',
+        f'    %10 = "arith.select"(%c, %x, %y) : ({Ti1}, {T32}, {T32}) -> {T32}',
+    ]
+    rets = [f"%{i}" for i in range(11)]
+    tys = [T32, T32, T32, F, F, F, Ti8, T32, Ti64, T32, T32]
+    text = ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({", ".join(tys)}), sym_name = "main"}}> ({{\n'
+            + "\n".join(lines) + f'\n    "func.return"({", ".join(rets)}) : ({", ".join(tys)}) -> ()\n'
+            '  }) : () -> ()\n}) : () -> ()\n')
+    out, st = opt.run(text, "canonicalize")
+    got = consts_returned(out)
+    assert all(d.name == "arith.constant" for d in got), [d.name for d in got]
+    t6 = oracle.convert("trunci", "i32", "i8", x).out
+    want = [oracle.binary("floordivsi", "i32", x, y).out, oracle.binary("ceildivsi", "i32", x, y).out,
+            oracle.binary("ceildivui", "i32", x, y).out, oracle.binary("remf", "f32", fa, fb).out,
+            oracle.convert("negf", "f32", "f32", fa).out, oracle.convert("flush_denormals", "f32", "f32", fb).out,
+            t6, oracle.convert("extsi", "i8", "i32", t6).out, oracle.convert("extsi", "i32", "i64", y).out,
+            fa, oracle.select(c, x, y).out]
+    for i, (d, w) in enumerate(zip(got, want)):
+        assert np.array_equal(full(d, n), w.astype(np.uint64)), i

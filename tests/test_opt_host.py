@@ -147,3 +147,61 @@ def test_split_input_file_and_generated_configs_parse():
     t = mlir_gen.config5_text(funcs=3, side=4, weight_side=0)
     with pytest.raises(opt.OptError, match="needs a GPU"):
         opt.run(t, mlir_gen.LAYERWISE, n_gpus=0)
+
+
+def test_bitcast_shares_bytes_without_element_work():
+    # bitcast keeps the bits under the new element type
+    # (src/patterns/arith/canonicalize.rs:764-789): the host-only engine
+    # folds it, with the large literal carried over as is.
+    n = 4096
+    hexs = b"".join((0x3F800000 + i).to_bytes(4, "little") for i in range(n)).hex().upper()
+    body = "\n".join([const("%0", f'dense<"0x{hexs}">', f"tensor<{n}xf32>"),
+                      f'    %1 = "arith.bitcast"(%0) : (tensor<{n}xf32>) -> tensor<{n}xi32>'])
+    out = run(module(body, "%1", f"tensor<{n}xi32>"))
+    f, d = returned(out)
+    assert d.name == "arith.constant" and d.const.ty.elem == "i32"
+    assert d.const.bits == [0x3F800000 + i for i in range(n)]
+
+
+def test_select_shortcuts():
+    c4 = "tensor<4xi1>"
+    body = "\n".join([const("%c", "dense<true>", c4), const("%0", C4, T), const("%1", "dense<0.0>", T),
+                      f'    %2 = "arith.select"(%c, %0, %1) : ({c4}, {T}, {T}) -> {T}'])
+    f, d = returned(run(module(body, "%2", T)))
+    assert d.name == "arith.constant" and d.const.bits == [0x3F800000, 0x40000000, 0x40400000, 0x40800000]
+    # select(c, x, x) -> x, with a non-constant condition
+    body = "\n".join([const("%0", C4, T),
+                      f'    %c = "test.cond"() : () -> {c4}',
+                      f'    %2 = "arith.select"(%c, %0, %0) : ({c4}, {T}, {T}) -> {T}'])
+    f, d = returned(run(module(body, "%2", T)))
+    assert d.name == "arith.constant"
+
+
+def test_ext_trunc_chains_fold_on_the_host():
+    i8, i32 = "tensor<4xi8>", "tensor<4xi32>"
+    body = "\n".join([f'    %x = "test.src"() : () -> {i8}',
+                      f'    %1 = "arith.extsi"(%x) : ({i8}) -> tensor<4xi16>',
+                      f'    %2 = "arith.extsi"(%1) : (tensor<4xi16>) -> {i32}',
+                      f'    %3 = "arith.trunci"(%2) : ({i32}) -> {i8}'])
+    # trunci(extsi(x)) back to x's type is x itself (:685-706)
+    f, d = returned(run(module(body, "%3", i8)))
+    assert d.name == "test.src"
+
+
+def test_new_element_folds_need_a_gpu():
+    i32 = "tensor<4xi32>"
+    body = "\n".join([const("%0", "dense<[7, -7, 9, 3]>", i32), const("%1", "dense<[2, 2, -4, 3]>", i32),
+                      f'    %2 = "arith.floordivsi"(%0, %1) : ({i32}, {i32}) -> {i32}'])
+    with pytest.raises(opt.OptError, match="needs a GPU"):
+        run(module(body, "%2", i32))
+
+
+def test_big_list_literals_are_constants():
+    # A literal list longer than the parser's in-place threshold (i1
+    # constants print as lists at any size) is still a constant.
+    n = 3000
+    lst = ", ".join(str(i) for i in range(n))
+    body = "\n".join([const("%0", f"dense<[{lst}]>", f"tensor<{n}xi32>"),
+                      f'    %1 = "arith.bitcast"(%0) : (tensor<{n}xi32>) -> tensor<{n}xf32>'])
+    f, d = returned(run(module(body, "%1", f"tensor<{n}xf32>")))
+    assert d.name == "arith.constant" and d.const.bits == list(range(n))

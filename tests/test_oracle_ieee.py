@@ -148,6 +148,8 @@ def test_minmax_rules(oracle):
 
 
 WIDTHS = {"i8": (np.int8, 8), "i16": (np.int16, 16), "i32": (np.int32, 32), "i64": (np.int64, 64)}
+STORAGE_OF = {"i1": np.uint8, "i8": np.uint8, "i16": np.uint16, "i32": np.uint32, "i64": np.uint64,
+              "f16": np.uint16, "bf16": np.uint16, "f32": np.uint32, "f64": np.uint64}
 
 
 def ints(dt, n, seed):
@@ -317,3 +319,106 @@ def test_hex_and_transpose(oracle):
     x = rng.integers(0, 1 << 16, size=(3, 5, 7), dtype=np.uint16)
     for perms in [(1, 0, 2), (2, 1, 0), (0, 2, 1), (2, 0, 1)]:
         assert np.array_equal(oracle.transpose(x, x.shape, perms), np.transpose(x, perms))
+
+
+def _sx(v, w):
+    return v - (1 << w) if v >> (w - 1) else v
+
+
+def _py_more(op, a, b, w):
+    """Python-integer statement of the rounding divisions, the high product
+    half and the addui carry (exact arithmetic, then the range check)."""
+    m = (1 << w) - 1
+    sa, sb = _sx(a, w), _sx(b, w)
+    lo, hi = -(1 << (w - 1)), (1 << (w - 1)) - 1
+    if op == "ceildivui":
+        return None if b == 0 else -(-a // b) & m
+    if op in ("ceildivsi", "floordivsi"):
+        if b == 0:
+            return None
+        q = -((-sa) // sb) if op == "ceildivsi" else sa // sb
+        if op == "ceildivsi" and sa != 0 and (sa == lo or sb == lo):
+            return None                      # an overflowing step of :557-595
+        if not lo <= q <= hi:
+            return None
+        return q & m
+    if op == "mulsi_hi":
+        return ((sa * sb) >> w) & m
+    if op == "mului_hi":
+        return ((a * b) >> w) & m
+    if op == "addui_carry":
+        return int(((a + b) & m) < a)
+    raise ValueError(op)
+
+
+@pytest.mark.parametrize("dt", ["i1", "i8", "i16", "i32", "i64"])
+@pytest.mark.parametrize("op", ["ceildivui", "ceildivsi", "floordivsi", "mulsi_hi", "mului_hi", "addui_carry"])
+def test_more_int_ops_match_python(op, dt, oracle):
+    w = {"i1": 1, "i8": 8, "i16": 16, "i32": 32, "i64": 64}[dt]
+    m = (1 << w) - 1
+    rng = np.random.default_rng(5)
+    vals = [0, 1, m, m - 1, 1 << (w - 1), (1 << (w - 1)) - 1] if w > 1 else [0, 1]
+    pairs = [(x, y) for x in vals for y in vals]
+    pairs += [(int(x) & m, int(y) & m) for x, y in rng.integers(0, 2**63, (400, 2), dtype=np.uint64)]
+    st = STORAGE_OF[dt]
+    for x, y in pairs:
+        want = _py_more(op, x, y, w)
+        f = oracle.binary(op, dt, np.array([x], st), np.array([y], st))
+        if want is None:
+            assert not f.folded, (op, dt, x, y)
+        else:
+            assert f.folded and int(f.out[0]) == want, (op, dt, x, y, int(f.out[0]), want)
+
+
+def test_ext_trunc_negf_flush(oracle):
+    x = np.array([0, 1, 0x7F, 0x80, 0xFF], np.uint8)
+    assert list(oracle.convert("extsi", "i8", "i32", x).out) == [0, 1, 0x7F, 0xFFFFFF80, 0xFFFFFFFF]
+    assert list(oracle.convert("extui", "i8", "i32", x).out) == [0, 1, 0x7F, 0x80, 0xFF]
+    assert list(oracle.convert("extsi", "i1", "i8", np.array([0, 1], np.uint8)).out) == [0, 0xFF]
+    y = np.array([0x12345678, 0xFFFFFF80], np.uint32)
+    assert list(oracle.convert("trunci", "i32", "i8", y).out) == [0x78, 0x80]
+    f = np.array([0x3F800000, 0x80000000, 0x7FC00001, 0x00000001, 0x807FFFFF, 0x00800000], np.uint32)
+    assert list(oracle.convert("negf", "f32", "f32", f).out) == [0xBF800000, 0, 0xFFC00001, 0x80000001, 0x007FFFFF,
+                                                                 0x80800000]
+    assert list(oracle.convert("flush_denormals", "f32", "f32", f).out) == [0x3F800000, 0x80000000, 0x7FC00001, 0,
+                                                                            0x80000000, 0x00800000]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64", "f16", "bf16"])
+def test_remf_matches_fmod(dt, oracle):
+    import math
+    rng = np.random.default_rng(9)
+    if dt in ("f32", "f64"):
+        npt = {"f32": np.float32, "f64": np.float64}[dt]
+        a = (rng.standard_normal(3000) * 1e3).astype(npt)
+        b = (rng.standard_normal(3000) * 10).astype(npt)
+        f = oracle.binary("remf", dt, a.view(STORAGE_OF[dt]), b.view(STORAGE_OF[dt]))
+        want = np.array([math.fmod(float(x), float(y)) for x, y in zip(a, b)], npt)
+        assert f.folded and np.array_equal(f.out, want.view(STORAGE_OF[dt]))
+    else:
+        a = rng.integers(0, 0x7C00, 3000, dtype=np.uint16)
+        b = rng.integers(0x0400, 0x7C00, 3000, dtype=np.uint16)
+        f = oracle.binary("remf", dt, a, b)
+        if dt == "f16":
+            want = [math.fmod(float(x), float(y)) for x, y in zip(a.view(np.float16), b.view(np.float16))]
+            assert np.array_equal(f.out, np.array(want, np.float16).view(np.uint16))
+        else:
+            wa = (a.astype(np.uint32) << 16).view(np.float32)
+            wb = (b.astype(np.uint32) << 16).view(np.float32)
+            want = np.array([math.fmod(float(x), float(y)) for x, y in zip(wa, wb)], np.float32)
+            assert not np.any(want.view(np.uint32) & 0xFFFF)   # exact in bf16
+            assert np.array_equal(f.out, (want.view(np.uint32) >> 16).astype(np.uint16))
+    # invalid and special operands
+    one, zero, inf = 0x3F800000, 0, 0x7F800000
+    got = oracle.binary("remf", "f32", np.array([inf, one, one, 0x7FC00005], np.uint32),
+                        np.array([one, zero, inf, one], np.uint32)).out
+    assert list(got) == [0x7FC00000, 0x7FC00000, one, 0x7FC00005]
+
+
+def test_select(oracle):
+    c = np.array([1, 0, 1, 0, 2], np.uint8)
+    t = np.arange(5, dtype=np.uint32)
+    e = np.arange(10, 15, dtype=np.uint32)
+    assert list(oracle.select(c, t, e).out) == [0, 11, 2, 13, 4]
+    f = oracle.select(np.array([0], np.uint8), t, np.array([7], np.uint32), n=5, cond_splat=True, f_splat=True)
+    assert list(f.out) == [7] * 5 and f.is_splat
