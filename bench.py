@@ -485,7 +485,10 @@ def run_kernels(args):
            reps=5)
     w = T(W.config5_weight().view(np.int16))
     wo = torch.empty_like(w)
-    timeit(lambda: dcf.transpose2d_async(2, 16384, 16384, w, wo), 4 * w.numel(), ("config5 16384x16384 bf16", "transpose"))
+    timeit(lambda: dcf.permute_async(2, (16384, 16384), (1, 0), w, wo, st), 4 * w.numel(),
+           ("config5 16384x16384 bf16", "transpose (bulk-tensor pipeline)"))
+    timeit(lambda: dcf.transpose2d_async(2, 16384, 16384, w, wo), 4 * w.numel(),
+           ("config5 16384x16384 bf16", "transpose (plain loads)"))
 
 
 def run_pass(args):
@@ -524,7 +527,8 @@ def run_pass(args):
             "text_memory": "pageable" if args.pageable else "pinned",
             "parse_ms": round(best["parse_ms"], 2), "run_ms": round(best["run_ms"], 3),
             "run_ms_mean": round(statistics.mean(s["run_ms"] for s in runs), 3),
-            "print_ms": round(best["print_ms"], 2), "wall_ms": round(best["wall_ms"], 1),
+            "print_ms": round(best["print_ms"], 2), "call_ms": round(best["call_ms"], 1),
+            "wall_ms": round(best["wall_ms"], 1),
             "upload_ms": round(best["upload_ms"], 2), "fold_ms": round(best["fold_ms"], 2),
             "download_ms": round(best["download_ms"], 2),
             "folds": best["folds"], "refused": best["refused"],

@@ -346,6 +346,15 @@ int dcf_permute_async(size_t elem_size, int rank, const int64_t* in_shape,
                       const int64_t* perms, const void* in, void* out,
                       void* stream);
 
+/* As dcf_permute_async, with a device status (reset it first).  Transposes
+ * of 2-byte elements (a swap of two groups of dims, both extents of the
+ * 2-D view multiples of 8, 16-byte aligned buffers) run as a bulk-tensor
+ * (TMA) pipeline whose bounded waits report through status->error. */
+int dcf_permute_status_async(size_t elem_size, int rank,
+                             const int64_t* in_shape, const int64_t* perms,
+                             const void* in, void* out, dcf_status* status,
+                             void* stream);
+
 /* Splat test on device memory: afterwards status->splat_word != 0 when all
  * n elements equal element 0 (the all-values test of Tf::splat,
  * src/patterns/tosa/canonicalize.rs:97-100).  Reset the status first. */
@@ -356,6 +365,29 @@ int dcf_hex_encode_async(const void* in, uint64_t nbytes, char* out,
                          void* stream);
 int dcf_hex_decode_async(const char* in, uint64_t nchars, void* out,
                          dcf_status* status, void* stream);
+
+/* One literal of a batched hex decode: nchars characters at `in` become
+ * nchars / 2 bytes at `out` (both device pointers). */
+typedef struct dcf_hex_piece {
+  const char* in;
+  void* out;
+  uint64_t nchars;
+} dcf_hex_piece;
+
+/* Decode n literals with one launch (per 65535 pieces).  `pieces` is a
+ * DEVICE array of n descriptors that the caller has written; max_nchars
+ * bounds every piece's nchars (it sizes the grid, so split very long
+ * literals into pieces of similar length).  A piece whose output is 8-byte
+ * aligned is decoded 16 characters per thread step at any text alignment;
+ * when its text is not 16-byte aligned the kernel reads the whole aligned
+ * 16-byte blocks around it, so up to 15 bytes before the text and 16 bytes
+ * after it must be readable device memory.  An invalid character or an odd
+ * length sets status->first_fail.  The literal-by-literal decode of many
+ * constants that a module parse needs, without one launch per constant.
+ * Reset the status first. */
+int dcf_hex_decode_many_async(const dcf_hex_piece* pieces, size_t n,
+                              uint64_t max_nchars, dcf_status* status,
+                              void* stream);
 
 /* Read a device dcf_status back into a dcf_result (synchronises stream). */
 int dcf_status_read(const dcf_status* status, void* stream, dcf_result* res);

@@ -114,9 +114,12 @@ SIGNATURES = {
     "dcf_transpose2d_async": (_I, [_SZ, _U64, _U64, _VP, _VP, _VP]),
     "dcf_permute_async": (_I, [_SZ, _I, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _VP, _VP,
                                _VP]),
+    "dcf_permute_status_async": (_I, [_SZ, _I, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _VP,
+                                      _VP, _VP, _VP]),
     "dcf_splat_check_async": (_I, [_VP, _SZ, _U64, _VP, _VP]),
     "dcf_hex_encode_async": (_I, [_VP, _U64, _VP, _VP]),
     "dcf_hex_decode_async": (_I, [_VP, _U64, _VP, _VP, _VP]),
+    "dcf_hex_decode_many_async": (_I, [_VP, _SZ, _U64, _VP, _VP]),
     "dcf_status_read": (_I, [_VP, _VP, _RP]),
 }
 
@@ -404,6 +407,16 @@ def select_async(cond, t, f, out, status, *, n: int | None = None, cond_splat: b
         n = out.numel()
     _check(lib().dcf_select_async(out.element_size(), _tptr(cond), int(cond_splat), _tptr(t), int(t_splat), _tptr(f),
                                   int(f_splat), n, _tptr(out), _tptr(status), _stream(stream)))
+
+
+def permute_async(elem_size: int, shape, perms, x, out, status, stream=None) -> None:
+    """dcf_permute_status_async on device tensors (2-byte transposes take the
+    bulk-tensor kernel)."""
+    rank = len(shape)
+    sh = (ctypes.c_int64 * rank)(*shape)
+    pm = (ctypes.c_int64 * rank)(*perms)
+    _check(lib().dcf_permute_status_async(elem_size, rank, sh, pm, _tptr(x), _tptr(out), _tptr(status),
+                                          _stream(stream)))
 
 
 def transpose2d_async(elem_size: int, rows: int, cols: int, x, out, stream=None) -> None:

@@ -443,6 +443,7 @@ __global__ void __launch_bounds__(kThreads) ew_batch_kernel(const BatchDesc* __r
 
 int grid_for(uint64_t work_items, const void* kernel);
 int sm_count_current();
+int tma_min_tiles_per_sm();
 bool prepare_smem(const void* kernel, int bytes);
 
 template <class F>
@@ -468,7 +469,7 @@ int launch_one(const EwLaunch& a) {
   const int streamed = (a.lsplat ? 0 : 1) + (F::kBinary && !a.rsplat ? 1 : 0);
   const uint64_t ntiles = a.n / (kTileBytes / sizeof(typename F::In));
   const int sms = sm_count_current();
-  if (vec && streamed > 0 && ntiles >= (uint64_t)sms * 2) {
+  if (vec && streamed > 0 && ntiles >= (uint64_t)sms * tma_min_tiles_per_sm()) {
     const int smem = kStages * kTileBytes * streamed + kStages * 8;
     if (!prepare_smem((const void*)ew_tma_kernel<F>, smem)) return DCF_ECUDA;
     const uint64_t g = ntiles < (uint64_t)sms * kTmaCtasPerSm ? ntiles : (uint64_t)sms * kTmaCtasPerSm;

@@ -71,12 +71,18 @@ int launch_int_binary(const EwLaunch& a);      // addi..minui, cmpi
 int launch_convert(const EwLaunch& a);         // extf, truncf, si/uitofp, fptosi/ui
 int launch_reciprocal(const EwLaunch& a);
 
+// With a status, 2-byte transposes take the bulk-tensor kernel when the
+// shapes and alignment allow (its bounded waits report through st->error).
 int launch_transpose2d(size_t elem_size, uint64_t rows, uint64_t cols, const void* in, void* out,
-                       cudaStream_t stream);
+                       cudaStream_t stream, dcf_status* st = nullptr);
+int launch_transpose2_tma(const void* in, void* out, uint64_t rows, uint64_t cols, dcf_status* st,
+                          cudaStream_t stream);
 int launch_permute(size_t elem_size, int rank, const int64_t* in_shape, const int64_t* perms,
-                   const void* in, void* out, cudaStream_t stream);
+                   const void* in, void* out, cudaStream_t stream, dcf_status* st = nullptr);
 int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t stream);
 int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st, cudaStream_t stream);
+int launch_hex_decode_pieces(const dcf_hex_piece* pieces, size_t n, uint64_t max_nchars, dcf_status* st,
+                             cudaStream_t stream);
 int launch_select(size_t elem_size, const void* cond, int cond_splat, const void* t, int t_splat, const void* f,
                   int f_splat, uint64_t n, void* out, dcf_status* st, cudaStream_t stream);
 int launch_splat_check(const void* in, size_t elem_size, uint64_t n, dcf_status* st, cudaStream_t stream);

@@ -1,7 +1,9 @@
 // dcf_misc.cu — dispatch, grid sizing, and the data-movement kernels:
 // transpose / permute (the layerwise transpose fold), the dense hex codec
 // (dense<"0x…"> bodies), and the splat test.
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -50,6 +52,18 @@ int grid_for(uint64_t work_items, const void* kernel) {
   uint64_t need = (work_items + (uint64_t)kThreads * kUnroll - 1) / ((uint64_t)kThreads * kUnroll);
   if (need < 1) need = 1;
   return (int)(need < resident ? need : resident);
+}
+
+// The bulk-copy pipeline pays a fixed cost per CTA (barrier set-up, the
+// first copies' latency, a partial last round); below this many 16 KB tiles
+// per SM the plain-load kernel is used.  DCF_TMA_TILES_PER_SM overrides it.
+int tma_min_tiles_per_sm() {
+  static const int v = [] {
+    const char* e = getenv("DCF_TMA_TILES_PER_SM");
+    const int x = e ? atoi(e) : 0;
+    return x > 0 ? x : 2;
+  }();
+  return v;
 }
 
 int sm_count_current() {
@@ -161,8 +175,13 @@ static int sm_count() {
   return n > 0 ? n : 1;
 }
 
-int launch_transpose2d(size_t es, uint64_t rows, uint64_t cols, const void* in, void* out, cudaStream_t st) {
+int launch_transpose2d(size_t es, uint64_t rows, uint64_t cols, const void* in, void* out, cudaStream_t st,
+                       dcf_status* status) {
   if (rows == 0 || cols == 0) return DCF_OK;
+  if (es == 2 && status) {
+    const int rc = launch_transpose2_tma(in, out, rows, cols, status, st);
+    if (rc != DCF_EUNSUPPORTED) return rc;
+  }
   const int sms = sm_count();
   if (es == 2 && rows % 64 == 0 && cols % 64 == 0 && ((uintptr_t)in & 3) == 0 && ((uintptr_t)out & 3) == 0) {
     const uint64_t nt = (rows / 64) * (cols / 64);
@@ -206,8 +225,20 @@ __global__ void __launch_bounds__(256) permute_kernel(const T* __restrict__ in, 
 }
 
 int launch_permute(size_t es, int rank, const int64_t* in_shape, const int64_t* perms, const void* in, void* out,
-                   cudaStream_t st) {
+                   cudaStream_t st, dcf_status* status) {
   if (rank < 1 || rank > 8) return DCF_EINVAL;
+  // A swap of two contiguous groups of dims is a 2-D transpose.
+  for (int split = 1; split < rank; split++) {
+    bool swap = true;
+    for (int i = 0; i < rank && swap; i++)
+      swap = perms[i] == ((i < rank - split) ? split + i : i - (rank - split));
+    if (swap) {
+      uint64_t rows = 1, cols = 1;
+      for (int i = 0; i < split; i++) rows *= (uint64_t)in_shape[i];
+      for (int i = split; i < rank; i++) cols *= (uint64_t)in_shape[i];
+      return launch_transpose2d(es, rows, cols, in, out, st, status);
+    }
+  }
   PermDesc d{};
   d.rank = rank;
   int64_t in_stride[8], total = 1;
@@ -273,12 +304,11 @@ __device__ __forceinline__ int unhex(uint32_t c) {
   return -1;
 }
 
-// 16 characters -> 8 bytes per thread; an invalid character records its
-// index as the status's first_fail.
-__global__ void __launch_bounds__(256) hex_decode_kernel(const char* __restrict__ in, uint64_t nbytes,
-                                                         uint8_t* __restrict__ out, dcf_status* st, int vec) {
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Decode nbytes bytes from 2*nbytes characters, threads tid, tid+stride,
+// ...: 16 characters -> 8 bytes per step when the text is 16-byte aligned
+// (vec).  Returns the lowest invalid character index this thread saw.
+__device__ __forceinline__ uint64_t decode_span(const char* __restrict__ in, uint64_t nbytes,
+                                                uint8_t* __restrict__ out, uint64_t tid, uint64_t stride, bool vec) {
   const uint64_t nv = vec ? nbytes / 8 : 0;
   uint64_t bad = ~0ull;
   for (uint64_t v = tid; v < nv; v += stride) {
@@ -306,6 +336,105 @@ __global__ void __launch_bounds__(256) hex_decode_kernel(const char* __restrict_
     }
     out[i] = (uint8_t)((h << 4 | l) & 0xFF);
   }
+  return bad;
+}
+
+// An invalid character records its index as the status's first_fail.
+__global__ void __launch_bounds__(256) hex_decode_kernel(const char* __restrict__ in, uint64_t nbytes,
+                                                         uint8_t* __restrict__ out, dcf_status* st, int vec) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  report(st, decode_span(in, nbytes, out, tid, stride, vec != 0), false);
+}
+
+// 16 characters (as four words) -> 8 bytes; `bad` gets the lowest invalid
+// character index, counting from `at`.
+__device__ __forceinline__ uint2 decode16(const uint32_t (&w)[4], uint64_t at, uint64_t& bad) {
+  uint32_t o[2] = {0, 0};
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t word = w[k / 2];
+    const uint32_t c0 = (word >> ((k & 1) * 16)) & 0xFF, c1 = (word >> ((k & 1) * 16 + 8)) & 0xFF;
+    const int h = unhex(c0), l = unhex(c1);
+    if (h < 0 || l < 0) {
+      const uint64_t x = at + 2 * k + (h < 0 ? 0 : 1);
+      bad = x < bad ? x : bad;
+    }
+    o[k / 4] |= (uint32_t)((h << 4 | l) & 0xFF) << ((k & 3) * 8);
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+// Text at any alignment m = in % 16: each lane loads the aligned 16-byte
+// block under its 16 characters, takes the next block from its neighbour
+// lane (the last lane loads it), and funnel-shifts the pair by m bytes.
+// Reads up to 15 bytes before the text and 16 bytes after its end.  The
+// loop runs whole warps (stride is a multiple of 32).
+__device__ __forceinline__ uint64_t decode_span_shifted(const char* __restrict__ in, uint64_t nbytes,
+                                                        uint8_t* __restrict__ out, uint64_t tid, uint64_t stride) {
+  const unsigned full = 0xFFFFFFFFu;
+  const int lane = threadIdx.x & 31;
+  const uint32_t m = (uint32_t)((uintptr_t)in & 15);
+  const uint4* base = (const uint4*)(in - m);
+  const uint64_t nv = nbytes / 8;
+  uint64_t bad = ~0ull;
+  for (uint64_t vb = tid - lane; vb < nv; vb += stride) {
+    const uint64_t v = vb + lane;
+    const uint4 cur = v < nv ? __ldg(base + v) : make_uint4(0, 0, 0, 0);
+    uint4 nxt;
+    nxt.x = __shfl_down_sync(full, cur.x, 1);
+    nxt.y = __shfl_down_sync(full, cur.y, 1);
+    nxt.z = __shfl_down_sync(full, cur.z, 1);
+    nxt.w = __shfl_down_sync(full, cur.w, 1);
+    if (lane == 31 || v + 1 >= nv) {
+      if (v < nv) nxt = __ldg(base + v + 1);
+    }
+    if (v < nv) {
+      const uint32_t w8[8] = {cur.x, cur.y, cur.z, cur.w, nxt.x, nxt.y, nxt.z, nxt.w};
+      const uint32_t sh = 8 * (m & 3);
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        uint32_t lo, hi;
+        switch (m >> 2) {  // whole words to skip
+          case 0: lo = w8[k]; hi = w8[k + 1]; break;
+          case 1: lo = w8[k + 1]; hi = w8[k + 2]; break;
+          case 2: lo = w8[k + 2]; hi = w8[k + 3]; break;
+          default: lo = w8[k + 3]; hi = w8[k + 4]; break;
+        }
+        w[k] = __funnelshift_r(lo, hi, sh);
+      }
+      *(uint2*)(out + v * 8) = decode16(w, v * 16, bad);
+    }
+  }
+  for (uint64_t i = nv * 8 + tid; i < nbytes; i += stride) {
+    const int h = unhex((uint8_t)in[2 * i]), l = unhex((uint8_t)in[2 * i + 1]);
+    if (h < 0 || l < 0) {
+      const uint64_t at = 2 * i + (h < 0 ? 0 : 1);
+      bad = at < bad ? at : bad;
+    }
+    out[i] = (uint8_t)((h << 4 | l) & 0xFF);
+  }
+  return bad;
+}
+
+// Many literals in one launch: blockIdx.y picks the piece, the blocks along
+// x stride over it.  An invalid character anywhere sets first_fail to the
+// lowest index within its piece.
+__global__ void __launch_bounds__(256) hex_decode_pieces_kernel(const dcf_hex_piece* __restrict__ pieces,
+                                                                dcf_status* st) {
+  const dcf_hex_piece pc = pieces[blockIdx.y];
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t bad = 0;
+  if (!(pc.nchars & 1)) {
+    if ((uintptr_t)pc.out & 7)
+      bad = decode_span(pc.in, pc.nchars / 2, (uint8_t*)pc.out, tid, stride, false);
+    else if ((uintptr_t)pc.in & 15)
+      bad = decode_span_shifted(pc.in, pc.nchars / 2, (uint8_t*)pc.out, tid, stride);
+    else
+      bad = decode_span(pc.in, pc.nchars / 2, (uint8_t*)pc.out, tid, stride, true);
+  }
   report(st, bad, false);
 }
 
@@ -330,6 +459,22 @@ int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st
   note_launch();
   hex_decode_kernel<<<g, 256, 0, st>>>(in, nbytes, (uint8_t*)out, status, vec);
   return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
+}
+
+int launch_hex_decode_pieces(const dcf_hex_piece* pieces, size_t n, uint64_t max_nchars, dcf_status* st,
+                             cudaStream_t s) {
+  if (n == 0) return DCF_OK;
+  // Blocks per piece: enough for the longest, at most 64; pieces go along y
+  // in launches of at most 65535.
+  const uint64_t vecs = max_nchars / 16 + 1;
+  const unsigned gx = (unsigned)std::min<uint64_t>(64, (vecs + 4 * 256 - 1) / (4 * 256));
+  for (size_t at = 0; at < n; at += 65535) {
+    const unsigned gy = (unsigned)std::min<size_t>(65535, n - at);
+    note_launch();
+    hex_decode_pieces_kernel<<<dim3(gx, gy), 256, 0, s>>>(pieces + at, st);
+    if (cudaPeekAtLastError() != cudaSuccess) return DCF_ECUDA;
+  }
+  return DCF_OK;
 }
 
 // --------------------------------------------------------------- select

@@ -646,23 +646,24 @@ int dcf_transpose(size_t elem_size, int rank, const int64_t* in_shape, const int
   }
   bool identity = true;
   for (int i = 0; i < rank; i++) identity = identity && perms[i] == i;
+  CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), s));
   if (identity) {
     CK(cudaMemcpyAsync(d.big[1], d.big[0], bytes, cudaMemcpyDeviceToDevice, s));
   } else if (swap2) {
-    rc = launch_transpose2d(elem_size, (uint64_t)rows, (uint64_t)cols, d.big[0], d.big[1], s);
+    rc = launch_transpose2d(elem_size, (uint64_t)rows, (uint64_t)cols, d.big[0], d.big[1], s, d.st);
   } else {
     rc = launch_permute(elem_size, rank, in_shape, perms, d.big[0], d.big[1], s);
   }
   if (rc) return set_err(rc, "transpose launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   if ((rc = d2h_full(d, out, d.big[1], bytes, s))) return rc;
   CK(cudaStreamSynchronize(s));
+  // A permutation keeps the multiset of values: splat in, splat out.  The
+  // same status carries the transpose's error word.
+  if ((rc = launch_splat_check(d.big[0], elem_size, total, d.st, s))) return rc;
+  dcf_status st;
+  if ((rc = read_status(d, s, &st))) return rc;
   if (res) {
     res->folded = 1;
-    // A permutation keeps the multiset of values: splat in, splat out.
-    CK(cudaMemsetAsync(d.st, 0xFF, sizeof(dcf_status), s));
-    if ((rc = launch_splat_check(d.big[0], elem_size, total, d.st, s))) return rc;
-    dcf_status st;
-    if ((rc = read_status(d, s, &st))) return rc;
     res->is_splat = st.splat_word != 0;
   }
   return DCF_OK;
@@ -1071,6 +1072,28 @@ int dcf_permute_async(size_t elem_size, int rank, const int64_t* in_shape, const
   return DCF_OK;
 }
 
+int dcf_permute_status_async(size_t elem_size, int rank, const int64_t* in_shape, const int64_t* perms,
+                             const void* in, void* out, dcf_status* status, void* stream) {
+  if (!status) return set_err(DCF_EINVAL, "null status");
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
+    return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
+  if (rank < 1 || rank > 8 || !in_shape || !perms) return set_err(DCF_EINVAL, "bad rank or shape");
+  uint64_t total = 1;
+  bool seen[8] = {false};
+  for (int i = 0; i < rank; i++) {
+    if (in_shape[i] < 0) return set_err(DCF_EINVAL, "negative dim");
+    if (perms[i] < 0 || perms[i] >= rank || seen[perms[i]]) return set_err(DCF_EINVAL, "perms is not a permutation");
+    seen[perms[i]] = true;
+    total *= (uint64_t)in_shape[i];
+  }
+  if (total == 0) return DCF_OK;
+  int rc = select_device(out);
+  if (rc) return rc;
+  rc = launch_permute(elem_size, rank, in_shape, perms, in, out, (cudaStream_t)stream, status);
+  if (rc) return set_err(rc, "permute launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return DCF_OK;
+}
+
 int dcf_splat_check_async(const void* in, size_t elem_size, uint64_t n, dcf_status* status, void* stream) {
   if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8)
     return set_err(DCF_EINVAL, "element size %zu not supported", elem_size);
@@ -1100,6 +1123,17 @@ int dcf_hex_decode_async(const char* in, uint64_t nchars, void* out, dcf_status*
   rc = launch_hex_decode(in, nchars, out, status, (cudaStream_t)stream);
   if (rc == DCF_EPARSE) return set_err(rc, "odd number of hex digits");
   if (rc) return set_err(rc, "hex decode launch failed");
+  return DCF_OK;
+}
+
+int dcf_hex_decode_many_async(const dcf_hex_piece* pieces, size_t n, uint64_t max_nchars, dcf_status* status,
+                              void* stream) {
+  if (n == 0) return DCF_OK;
+  if (!pieces || !status) return set_err(DCF_EINVAL, "null pointer");
+  int rc = select_device(pieces);
+  if (rc) return rc;
+  rc = launch_hex_decode_pieces(pieces, n, max_nchars, status, (cudaStream_t)stream);
+  if (rc) return set_err(rc, "hex decode launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   return DCF_OK;
 }
 

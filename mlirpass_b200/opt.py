@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import time
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdcfold_opt.so")
@@ -90,8 +91,10 @@ def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as
     out = ctypes.c_void_p()
     n = ctypes.c_size_t()
     st = Stats()
+    t0 = time.perf_counter()
     rc = lib().dcf_opt_run(addr, size, pipeline.encode(), n_gpus, int(split_input_file), ctypes.byref(out),
                            ctypes.byref(n), ctypes.byref(st))
+    call_ms = (time.perf_counter() - t0) * 1e3
     del keep
     if rc != 0:
         raise OptError(lib().dcf_opt_last_error().decode())
@@ -101,4 +104,6 @@ def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as
         b = bytes((ctypes.c_char * n.value).from_address(out.value)) if n.value else b""
     finally:
         lib().dcf_opt_free(out)
-    return (b if as_bytes else b.decode()), st.as_dict()
+    d = st.as_dict()
+    d["call_ms"] = call_ms
+    return (b if as_bytes else b.decode()), d

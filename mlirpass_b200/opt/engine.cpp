@@ -149,6 +149,85 @@ class CopyPool {
   }
 };
 
+// Page-locked host memory for constants' host bytes (installed as the
+// HostAllocator of ir.h).  Sizes are rounded to a power of two (64 KiB ...
+// 32 MiB, carved from 256 MiB slabs) or to 2 MiB (larger, own allocation);
+// freed blocks are kept per size and handed out again, so after the first
+// run a pipeline's results land in memory that is already pinned and
+// touched.  Allocation failures fall back to ordinary memory.
+class PinnedPool {
+ public:
+  static PinnedPool& get() {
+    static PinnedPool* p = new PinnedPool;  // never destroyed: buffers may be freed during exit
+    return *p;
+  }
+  void* alloc(size_t n) {
+    const size_t c = cls(n);
+    std::lock_guard<std::mutex> g(mu_);
+    auto& fl = free_[c];
+    if (!fl.empty()) {
+      void* p = fl.back();
+      fl.pop_back();
+      return p;
+    }
+    void* p = nullptr;
+    if (c <= kMaxSlabbed) {
+      if (left_ < c) {
+        if (cudaHostAlloc((void**)&cur_, kSlab, cudaHostAllocPortable) != cudaSuccess) {
+          cudaGetLastError();
+          cur_ = nullptr;
+          left_ = 0;
+          return ::operator new(n);
+        }
+        ranges_.emplace_back((uintptr_t)cur_, (uintptr_t)cur_ + kSlab);
+        left_ = kSlab;
+      }
+      p = cur_;
+      cur_ += c;
+      left_ -= c;
+      return p;
+    }
+    if (cudaHostAlloc(&p, c, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return ::operator new(n);
+    }
+    ranges_.emplace_back((uintptr_t)p, (uintptr_t)p + c);
+    return p;
+  }
+  void release(void* p, size_t n) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (owned_locked(p)) free_[cls(n)].push_back(p);
+    else ::operator delete(p);
+  }
+  bool owned(const void* p) {
+    std::lock_guard<std::mutex> g(mu_);
+    return owned_locked(p);
+  }
+
+ private:
+  static constexpr size_t kSlab = 256u << 20;
+  static constexpr size_t kMaxSlabbed = 32u << 20;
+  std::mutex mu_;
+  std::unordered_map<size_t, std::vector<void*>> free_;
+  std::vector<std::pair<uintptr_t, uintptr_t>> ranges_;
+  char* cur_ = nullptr;
+  size_t left_ = 0;
+  static size_t cls(size_t n) {
+    if (n > kMaxSlabbed) return (n + (2u << 20) - 1) & ~(size_t)((2u << 20) - 1);
+    size_t c = kHostPoolMin;
+    while (c < n) c <<= 1;
+    return c;
+  }
+  bool owned_locked(const void* p) const {
+    for (auto& r : ranges_)
+      if ((uintptr_t)p >= r.first && (uintptr_t)p < r.second) return true;
+    return false;
+  }
+};
+
+void* pinned_alloc(size_t n) { return PinnedPool::get().alloc(n); }
+void pinned_free(void* p, size_t n) { PinnedPool::get().release(p, n); }
+
 // Run fn(0..n-1) over the copy pool and wait.
 template <class F>
 void parallel(int n, F&& fn) {
@@ -205,6 +284,11 @@ DeviceBuf::~DeviceBuf() {
 Engine::Engine(int device) : dev_(device) {
   if (dev_ < 0) return;  // host-only: no element work
   ck(cudaSetDevice(dev_), "cudaSetDevice");
+  static std::once_flag once;
+  std::call_once(once, [] {
+    host_allocator().alloc = pinned_alloc;
+    host_allocator().free = pinned_free;
+  });
   ck(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking), "cudaStreamCreate");
 }
 
@@ -395,14 +479,16 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
   size_t total = 0, total_direct = 0;
   for (DenseValue* v : vs) {
     if (v->poison) throw std::runtime_error("a poison value has no bytes");
-    if (!v->host.empty()) {
+    if (!v->host.empty() && PinnedPool::get().owned(v->host.data())) {
+      direct.push_back({(void*)v->host.data(), nullptr, v->bytes(), total_direct});
+      raw.push_back({v, true, total_direct});
+      total_direct = align16(total_direct + v->bytes());
+    } else if (!v->host.empty()) {
       staged.push_back({(void*)v->host.data(), nullptr, v->bytes(), total});
       raw.push_back({v, false, total});
       total = align16(total + v->bytes());
     } else if (!v->hex.empty() && in_pinned(v->hex.data(), v->hex.size())) {
-      direct.push_back({(void*)v->hex.data(), nullptr, v->hex.size(), total_direct});
-      text.push_back({v, true, total_direct});
-      total_direct = align16(total_direct + v->hex.size());
+      text.push_back({v, true, 0});  // placed below, with its neighbours in the input
     } else if (!v->hex.empty()) {
       staged.push_back({(void*)v->hex.data(), nullptr, v->hex.size(), total});
       text.push_back({v, false, total});
@@ -414,12 +500,48 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
   std::vector<std::shared_ptr<DeviceBuf>> bufs(vs.size());
   for (size_t i = 0; i < vs.size(); i++) bufs[i] = std::make_shared<DeviceBuf>(dev_, vs[i]->bytes());
   auto buf_of = [&](DenseValue* v) -> std::shared_ptr<DeviceBuf>& { return bufs[index.at(v)]; };
+  // Literals inside the page-locked input are copied as runs: literals whose
+  // gaps in the input are short go in one copy with the text between them,
+  // 16 bytes of context on each side (the decoder reads whole aligned
+  // 16-byte blocks around a literal), placed so that device and host
+  // addresses agree modulo 16.
+  struct Run {
+    const char* a;
+    const char* b;
+    size_t off;
+  };
+  std::vector<Run> runs;
+  {
+    constexpr size_t kGap = 64u << 10, kCtx = 16;
+    std::vector<Loc*> order;
+    for (Loc& l : text)
+      if (l.is_direct) order.push_back(&l);
+    std::sort(order.begin(), order.end(), [](const Loc* x, const Loc* y) { return x->v->hex.data() < y->v->hex.data(); });
+    total_direct = std::max<size_t>(total_direct, kCtx);
+    for (Loc* l : order) {
+      const char* a = std::max(l->v->hex.data() - kCtx, pinned_src_);
+      const char* b = std::min(l->v->hex.data() + l->v->hex.size() + kCtx, pinned_src_ + pinned_len_);
+      if (!runs.empty() && a <= runs.back().b + kGap) {
+        runs.back().b = std::max(runs.back().b, b);
+      } else {
+        const size_t off = align16(total_direct) + ((uintptr_t)a & 15);
+        runs.push_back({a, b, off});
+      }
+      total_direct = runs.back().off + (size_t)(runs.back().b - runs.back().a) + kCtx;
+      l->off = runs.back().off + (size_t)(l->v->hex.data() - runs.back().a);
+    }
+  }
   std::unique_ptr<DeviceBuf> arena, arena_direct;
-  if (total_direct) {
-    arena_direct = std::make_unique<DeviceBuf>(dev_, total_direct);
+  if (!direct.empty() || !runs.empty()) {
+    arena_direct = std::make_unique<DeviceBuf>(dev_, total_direct + 32);
     for (const ImagePiece& p : direct)
       ck(cudaMemcpyAsync((char*)arena_direct->ptr + p.off, p.host, p.len, cudaMemcpyHostToDevice, s_), "H2D");
-    stats.h2d_bytes += total_direct;
+    for (const Run& r : runs) {
+      ck(cudaMemcpyAsync((char*)arena_direct->ptr + r.off, r.a, (size_t)(r.b - r.a), cudaMemcpyHostToDevice, s_),
+         "H2D");
+      stats.h2d_bytes += (size_t)(r.b - r.a);
+    }
+    for (const ImagePiece& p : direct) stats.h2d_bytes += p.len;
   }
   if (total) {
     arena = std::make_unique<DeviceBuf>(dev_, total);
@@ -431,8 +553,27 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
   if (!aux_) aux_ = std::make_unique<DeviceBuf>(dev_, sizeof(dcf_status));
   dcf_status* st = (dcf_status*)aux_->ptr;
   check(dcf_status_reset_async(st, s_), "status reset");
-  for (const Loc& l : text)
-    check(dcf_hex_decode_async(at(l), l.v->hex.size(), buf_of(l.v)->ptr, st, s_), "hex decode");
+  // Every literal is decoded by one batched launch; long literals are cut
+  // into pieces of at most kPieceChars characters so the grid stays even.
+  constexpr uint64_t kPieceChars = 4u << 20;
+  std::vector<dcf_hex_piece> pieces;
+  uint64_t max_chars = 0;
+  for (const Loc& l : text) {
+    const uint64_t nchars = l.v->hex.size();
+    for (uint64_t c = 0; c < nchars; c += kPieceChars) {
+      const uint64_t len = std::min<uint64_t>(kPieceChars, nchars - c);
+      pieces.push_back({at(l) + c, (char*)buf_of(l.v)->ptr + c / 2, len});
+      max_chars = std::max(max_chars, len);
+    }
+  }
+  std::unique_ptr<DeviceBuf> pdesc;
+  if (!pieces.empty()) {
+    pdesc = std::make_unique<DeviceBuf>(dev_, pieces.size() * sizeof(dcf_hex_piece));
+    ck(cudaMemcpyAsync(pdesc->ptr, pieces.data(), pieces.size() * sizeof(dcf_hex_piece), cudaMemcpyHostToDevice, s_),
+       "H2D pieces");
+    check(dcf_hex_decode_many_async((const dcf_hex_piece*)pdesc->ptr, pieces.size(), max_chars, st, s_),
+          "hex decode");
+  }
   for (const Loc& l : raw)
     ck(cudaMemcpyAsync(buf_of(l.v)->ptr, at(l), l.v->bytes(), cudaMemcpyDeviceToDevice, s_), "D2D");
   for (DenseValue* v : vs)
@@ -464,14 +605,23 @@ void Engine::to_host_all(const std::vector<DenseValue*>& in) {
     if (!v->dev || v->dev->device != dev_) off_device.push_back(v);
   to_device_all(off_device);
   set_device();
+  // Host bytes in page-locked memory take the copy straight from HBM; the
+  // rest go through the staging slots.
   std::vector<ImagePiece> pcs;
-  size_t total = 0;
+  size_t total = 0, direct = 0;
   for (DenseValue* v : vs) {
     if (v->host.data() == nullptr || v->host.size() != v->bytes()) v->host.resize(v->bytes());
+    if (PinnedPool::get().owned(v->host.data())) {
+      ck(cudaMemcpyAsync(v->host.data(), v->dev->ptr, v->bytes(), cudaMemcpyDeviceToHost, s_), "D2H");
+      direct += v->bytes();
+      continue;
+    }
     pcs.push_back({v->host.data(), v->dev->ptr, v->bytes(), total});
     total = align16(total + v->bytes());
   }
+  stats.d2h_bytes += direct;
   download_image(pcs, total);
+  sync();
   stats.download_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
 
@@ -716,7 +866,8 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
               "reciprocal fold");
         break;
       case FoldRequest::PERMUTE:
-        check(dcf_permute_async(oes, (int)q.shape.size(), q.shape.data(), q.perms.data(), l, outs[i]->ptr, s_),
+        check(dcf_permute_status_async(oes, (int)q.shape.size(), q.shape.data(), q.perms.data(), l, outs[i]->ptr,
+                                       st + i, s_),
               "transpose fold");
         break;
       case FoldRequest::SPLAT_SCAN:

@@ -17,6 +17,11 @@
 
 namespace dco {
 
+HostAllocator& host_allocator() {
+  static HostAllocator a;
+  return a;
+}
+
 // ================================================================== types
 
 static int dtype_of_elem(const std::string& e) {
@@ -405,7 +410,7 @@ void flatten_list(const std::string& s, std::vector<std::string>& out) {
 
 class Parser {
  public:
-  Parser(std::string_view s, Module& m) : s_(s), m_(m) {}
+  Parser(std::string_view s, Module& m) : s_(s), m_(m) { find_hex_literals(); }
 
   Op* parse_top() {
     scopes_.emplace_back();
@@ -466,6 +471,51 @@ class Parser {
     return trim(sub(r.first, r.second - r.first));
   }
 
+  // Hex literals ("0x... right after `dense<`): [opening quote, closing
+  // quote] positions, found up front by several threads, so that the
+  // sequential parse jumps over their bodies instead of scanning them.
+  // Inside another string a quote is escaped, so the pattern marks real
+  // literals only.
+  std::vector<std::pair<size_t, size_t>> lits_;
+  size_t lit_i_ = 0;
+
+  void find_hex_literals() {
+    constexpr size_t kMinText = 64u << 20;
+    if (s_.size() < kMinText) return;
+    const unsigned nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<std::vector<std::pair<size_t, size_t>>> part(nth);
+    auto scan = [&](unsigned t) {
+      const char* base = s_.data();
+      const size_t n = s_.size();
+      size_t p = n * t / nth;
+      const size_t end = n * (t + 1) / nth;
+      while (p < end) {
+        const char* q = (const char*)memchr(base + p, '"', end - p);
+        if (!q) break;
+        const size_t at = (size_t)(q - base);
+        if (at >= 6 && at + 2 < n && memcmp(q - 6, "dense<", 6) == 0 && q[1] == '0' && q[2] == 'x') {
+          const char* e = (const char*)memchr(q + 1, '"', n - at - 1);
+          if (!e) break;
+          part[t].emplace_back(at, (size_t)(e - base));
+          p = (size_t)(e - base) + 1;
+        } else {
+          p = at + 1;
+        }
+      }
+    };
+    std::vector<std::thread> th;
+    for (unsigned t = 1; t < nth; t++) th.emplace_back(scan, t);
+    scan(0);
+    for (auto& x : th) x.join();
+    for (auto& v : part) lits_.insert(lits_.end(), v.begin(), v.end());
+  }
+
+  // The closing quote of the hex literal opening at `at`, or npos.
+  size_t hex_literal_end(size_t at) {
+    while (lit_i_ < lits_.size() && lits_[lit_i_].first < at) lit_i_++;
+    return (lit_i_ < lits_.size() && lits_[lit_i_].first == at) ? lits_[lit_i_].second : std::string_view::npos;
+  }
+
   // The same, as [start, end) offsets: nothing is copied, and string
   // literals (the hex payload of a dense constant) are skipped with memchr.
   std::pair<size_t, size_t> span_pos(const char* stops) {
@@ -492,7 +542,11 @@ class Parser {
         continue;
       }
       if (depth == 0 && strchr(stops, c)) break;
-      if (c == '"') str = true;
+      if (c == '"') {
+        const size_t e = lits_.empty() ? std::string_view::npos : hex_literal_end(p_);
+        if (e != std::string_view::npos) p_ = e;  // at the closing quote; the string is done
+        else str = true;
+      }
       else if (c == '-' && p_ + 1 < s_.size() && s_[p_ + 1] == '>') p_++;
       else if (c == '(' || c == '[' || c == '{' || c == '<') depth++;
       else if (c == ')' || c == ']' || c == '}' || c == '>') {

@@ -49,6 +49,18 @@ class DeviceBuf;  // engine.h
 // Host bytes of a constant.  resize() leaves new bytes uninitialised: they
 // are always overwritten by a download or a decode, and zero-filling a
 // multi-GiB result first would cost as much as the copy itself.
+// Large host byte buffers come from a replaceable allocator: the engine
+// installs a page-locked caching pool, so that copies between a constant's
+// host bytes and the GPU need no staging, and the pages are reused from
+// run to run.  free() must accept memory it did not hand out (buffers
+// allocated before the pool was installed).
+struct HostAllocator {
+  void* (*alloc)(size_t bytes) = nullptr;
+  void (*free)(void* p, size_t bytes) = nullptr;
+};
+HostAllocator& host_allocator();
+constexpr size_t kHostPoolMin = 64u << 10;
+
 template <class T>
 struct NoInit : std::allocator<T> {
   template <class U>
@@ -58,6 +70,16 @@ struct NoInit : std::allocator<T> {
   NoInit() = default;
   template <class U>
   NoInit(const NoInit<U>&) noexcept {}
+  T* allocate(size_t n) {
+    const HostAllocator& h = host_allocator();
+    if (n * sizeof(T) >= kHostPoolMin && h.alloc) return (T*)h.alloc(n * sizeof(T));
+    return std::allocator<T>::allocate(n);
+  }
+  void deallocate(T* p, size_t n) {
+    const HostAllocator& h = host_allocator();
+    if (n * sizeof(T) >= kHostPoolMin && h.free) return h.free(p, n * sizeof(T));
+    std::allocator<T>::deallocate(p, n);
+  }
   template <class U>
   void construct(U* p) noexcept {
     ::new ((void*)p) U;

@@ -264,3 +264,15 @@ def test_more_arith_folds_through_canonicalize(oracle):
             fa, oracle.select(c, x, y).out]
     for i, (d, w) in enumerate(zip(got, want)):
         assert np.array_equal(full(d, n), w.astype(np.uint64)), i
+
+
+def test_pinned_text_gives_the_same_module():
+    # From page-locked text the driver copies runs of literals straight
+    # into HBM and decodes them at whatever alignment they have; the
+    # printed module must equal the one from ordinary memory.
+    text = mlir_gen.config5_text(40, 64, 256) + " " * 5     # odd sizes shift every literal's alignment
+    a, sa = opt.run(text, mlir_gen.LAYERWISE)
+    b, sb = opt.run(opt.pinned_text(text), mlir_gen.LAYERWISE)
+    assert a == b and sa["folds"] == sb["folds"] == 3 * 40 + 1
+    t2 = mlir_gen.config2_text(512)
+    assert opt.run(t2, "canonicalize")[0] == opt.run(opt.pinned_text(t2), "canonicalize")[0]

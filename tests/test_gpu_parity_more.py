@@ -100,3 +100,79 @@ def test_new_ops_through_the_device_api(dcf, oracle):
     assert dcf.status_read(st).folded
     want = oracle.select(c.cpu().numpy(), a, b)
     assert np.array_equal(out.cpu().numpy().view(np.uint32), want.out)
+
+
+def test_hex_decode_many(dcf, oracle):
+    # Many literals in one launch, aligned and unaligned, against the
+    # oracle's decoder; a bad digit in any piece is reported.
+    import ctypes
+    import torch
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(3)
+    sizes = [0, 1, 7, 8, 9, 100, 4096, 65537, 1 << 20]
+    raws = [rng.integers(0, 256, n, dtype=np.uint8) for n in sizes]
+    texts = [oracle.hex_encode(r.tobytes()) for r in raws]
+    offs, total = [], 0
+    for i, t in enumerate(texts):
+        total += (i % 3)                     # some pieces start unaligned
+        offs.append(total)
+        total += len(t) + 16
+    blob = np.zeros(total, dtype=np.uint8)
+    for o, t in zip(offs, texts):
+        blob[o:o + len(t)] = np.frombuffer(t, dtype=np.uint8)
+    dtext = torch.from_numpy(blob).to(dev)
+    outs = [torch.zeros(max(1, len(r)), dtype=torch.uint8, device=dev) for r in raws]
+
+    class Piece(ctypes.Structure):
+        _fields_ = [("in_", ctypes.c_void_p), ("out", ctypes.c_void_p), ("nchars", ctypes.c_uint64)]
+    arr = (Piece * len(raws))()
+    for i, (o, t) in enumerate(zip(offs, texts)):
+        arr[i].in_, arr[i].out, arr[i].nchars = dtext.data_ptr() + o, outs[i].data_ptr(), len(t)
+    dpieces = torch.from_numpy(np.frombuffer(bytes(arr), dtype=np.uint8).copy()).to(dev)
+    st = torch.empty(16, dtype=torch.uint8, device=dev)
+    dcf.status_reset(st)
+    assert dcf.lib().dcf_hex_decode_many_async(dpieces.data_ptr(), len(raws), max(len(t) for t in texts),
+                                               st.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
+    assert dcf.status_read(st).folded
+    for r, o in zip(raws, outs):
+        assert np.array_equal(o.cpu().numpy()[:len(r)], r)
+    blob2 = blob.copy()
+    blob2[offs[5] + 17] = ord("g")
+    dtext.copy_(torch.from_numpy(blob2))
+    dcf.status_reset(st)
+    assert dcf.lib().dcf_hex_decode_many_async(dpieces.data_ptr(), len(raws), max(len(t) for t in texts),
+                                               st.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
+    assert not dcf.status_read(st).folded
+
+
+@pytest.mark.parametrize("shape", [(8, 8), (64, 64), (72, 136), (136, 72), (1024, 8), (8, 1024), (2048, 4096),
+                                   (4104, 520)])
+def test_bulk_tensor_transpose(shape, dcf):
+    # 2-byte transposes whose extents are multiples of 8 run as the TMA
+    # pipeline (partial 64 x 64 edge tiles included); bit-exact against numpy.
+    import torch
+    rng = np.random.default_rng(shape[0] * 7 + shape[1])
+    w = rng.integers(0, 1 << 16, shape, dtype=np.uint16)
+    f = dcf.transpose(w, shape, (1, 0))
+    assert np.array_equal(f.out, w.T)
+    dev = torch.device("cuda:0")
+    tin = torch.from_numpy(w.view(np.int16)).to(dev)
+    tout = torch.empty(shape[1], shape[0], dtype=torch.int16, device=dev)
+    st = torch.empty(16, dtype=torch.uint8, device=dev)
+    dcf.status_reset(st)
+    import ctypes
+    sh = (ctypes.c_int64 * 2)(*shape)
+    pm = (ctypes.c_int64 * 2)(1, 0)
+    assert dcf.lib().dcf_permute_status_async(2, 2, sh, pm, tin.data_ptr(), tout.data_ptr(), st.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert dcf.status_read(st).folded
+    assert np.array_equal(tout.cpu().numpy().view(np.uint16), w.T)
+
+
+def test_permute_groups_take_the_transpose(dcf, oracle):
+    # A rank-3 permutation that swaps two groups of dims is a 2-D transpose.
+    x = np.arange(16 * 24 * 8, dtype=np.uint16).reshape(16, 24, 8)
+    for perms in [(1, 2, 0), (2, 0, 1), (0, 2, 1)]:
+        f = dcf.transpose(x, x.shape, perms)
+        assert np.array_equal(f.out, oracle.transpose(x, x.shape, perms)), perms
