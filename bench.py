@@ -491,6 +491,51 @@ def run_kernels(args):
            ("config5 16384x16384 bf16", "transpose (plain loads)"))
 
 
+def run_profile_kernels(args):
+    """One launch per round (two rounds) of the kernels profiled with ncu:
+    truncf f32->bf16, fptosi f32->i32, addi i8, the batched addf of 1024
+    256x256 functions, and the 16384x16384 bf16 transpose (bulk-tensor and
+    plain-load kernels).  Operands are device-resident and larger than L2;
+    nothing is timed here (the numbers come from the profiler)."""
+    import torch
+    import mlirpass_b200 as dcf
+    torch.cuda.set_device(0)
+    os.environ["DCF_DEVICES"] = "0"
+    dcf.init(1)
+    dev = torch.device("cuda", 0)
+    n = 64 << 20
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    x = torch.randn(n, device=dev, generator=g) * 1e3
+    xr = (x.view(torch.int32) & ~0xFFFF).view(torch.float32)          # bf16-representable
+    xi = x.clamp(-2e9, 2e9)
+    a8 = torch.randint(-128, 127, (n,), dtype=torch.int8, device=dev, generator=g)
+    b8 = torch.randint(-128, 127, (n,), dtype=torch.int8, device=dev, generator=g)
+    w = torch.randint(-30000, 30000, (16384, 16384), dtype=torch.int16, device=dev, generator=g)
+    o16 = torch.empty(n, dtype=torch.int16, device=dev)
+    o32 = torch.empty(n, dtype=torch.int32, device=dev)
+    o8 = torch.empty(n, dtype=torch.int8, device=dev)
+    wo = torch.empty_like(w)
+    st = torch.empty(2, dtype=torch.int64, device=dev)
+    A = [torch.rand(65536, device=dev, generator=g) for _ in range(1024)]
+    B = [torch.rand(65536, device=dev, generator=g) for _ in range(1024)]
+    O = [torch.empty(65536, device=dev) for _ in range(1024)]
+    tab = dcf.device_jobs([{"op": "addf", "dtype": "f32", "lhs": A[i], "rhs": B[i], "out": O[i]} for i in range(1024)])
+    for _ in range(2):
+        dcf.run_device_jobs(tab)
+        dcf.status_reset(st)
+        dcf.convert_async("truncf", "f32", "bf16", xr, o16, st)
+        dcf.status_reset(st)
+        dcf.convert_async("fptosi", "f32", "i32", xi, o32, st)
+        dcf.status_reset(st)
+        dcf.binary_async("addi", "i8", a8, b8, o8, st)
+        dcf.status_reset(st)
+        dcf.permute_async(2, (16384, 16384), (1, 0), w, wo, st)
+        dcf.transpose2d_async(2, 16384, 16384, w, wo)
+    torch.cuda.synchronize()
+    print(json.dumps({"workload": "profile-kernels", "launch_rounds": 2}))
+
+
 def run_pass(args):
     """A whole pipeline through the pass driver on MLIR text: parse / run /
     print phases, like the reference's own bench (fuzz/src/bench.rs:55-66)."""
@@ -517,7 +562,7 @@ def run_pass(args):
     runs = []
     for r in range(max(1, args.warmup) + args.steps):
         t0 = time.perf_counter()
-        out, st = opt.run(src, pipe, n_gpus=args.gpus, as_bytes=True)
+        out, st = opt.run(src, pipe, n_gpus=args.gpus, as_array=True)
         st["wall_ms"] = (time.perf_counter() - t0) * 1e3
         del out
         if r >= max(1, args.warmup):
@@ -546,7 +591,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="chain4096",
-                    help="chain4096 (the headline line), kernels, or pass:<config1|config2|config3-i8|...|config5>")
+                    help="chain4096 (the headline line), kernels, profile-kernels, or "
+                         "pass:<config1|config2|config3-i8|...|config5>")
     ap.add_argument("--funcs", type=int, default=4096, help="functions of config 5")
     ap.add_argument("--pageable", action="store_true", help="pass workloads: keep the module text in pageable memory")
     args = ap.parse_args()
@@ -554,6 +600,9 @@ def main():
         args.warmup = 3
     if args.workload == "kernels":
         run_kernels(args)
+        return
+    if args.workload == "profile-kernels":
+        run_profile_kernels(args)
         return
     if args.workload.startswith("pass:"):
         run_pass(args)

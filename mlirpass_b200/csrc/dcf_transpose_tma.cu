@@ -4,8 +4,8 @@
 // A rows x cols row-major matrix is cut into 64 x 64 tiles.  Persistent
 // CTAs walk the tiles; each tile arrives in shared memory by one
 // cp.async.bulk.tensor.2d load (a 64-element = 128-byte inner box with the
-// 128-byte swizzle) on a two-stage mbarrier pipeline, so the next tile is
-// in flight while this one is written out.  Eight lanes read an 8 x 8 block
+// 128-byte swizzle) on a four-stage mbarrier pipeline, so the next tiles
+// are in flight while this one is written out.  Eight lanes read an 8 x 8 block
 // as eight 16-byte rows (the swizzle puts the eight rows of a block in
 // eight different bank groups, so the reads are conflict-free), transpose
 // it in registers with three butterfly rounds of warp shuffles, and each
@@ -24,8 +24,7 @@ namespace {
 
 constexpr int kT = 64;                        // tile side (elements)
 constexpr int kTileBytes2 = kT * kT * 2;      // 8 KiB
-constexpr int kStages2 = 2;
-constexpr long kWaitLimit2 = 1l << 24;
+constexpr int kStages2 = 4;
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -83,10 +83,12 @@ def pinned_text(text):
     return t
 
 
-def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as_bytes: bool = False):
+def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as_bytes: bool = False,
+        as_array: bool = False):
     """Run `pipeline` over `text` (str, bytes, or a uint8 buffer such as
     pinned_text's); returns (printed module, stats dict).  The module is
-    str, or bytes with as_bytes=True."""
+    str, bytes with as_bytes=True, or with as_array=True a numpy uint8 view
+    of the driver's own output buffer (no copy; freed with the array)."""
     addr, size, keep = _buffer(text)
     out = ctypes.c_void_p()
     n = ctypes.c_size_t()
@@ -98,6 +100,17 @@ def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as
     del keep
     if rc != 0:
         raise OptError(lib().dcf_opt_last_error().decode())
+    if as_array:
+        import weakref
+        import numpy as np
+        # The finaliser hangs on the base array: every view of it (this
+        # slice included) keeps the buffer alive.
+        base = np.ctypeslib.as_array((ctypes.c_uint8 * max(1, n.value)).from_address(out.value))
+        weakref.finalize(base, lib().dcf_opt_free, out.value)
+        arr = base[:n.value]
+        d = st.as_dict()
+        d["call_ms"] = call_ms
+        return arr, d
     try:
         # ctypes.string_at takes a C int size: copy through a sized array so
         # outputs above 2 GiB work.

@@ -300,7 +300,7 @@ Engine::~Engine() {
     cudaStreamDestroy(s_);
   }
   for (int k = 0; k < kSlots; k++) {
-    if (pinned_[k]) cudaFreeHost(pinned_[k]);
+    if (pinned_[k]) PinnedPool::get().release(pinned_[k], kSlotBytes);
     if (slot_ev_[k]) cudaEventDestroy(slot_ev_[k]);
   }
 }
@@ -308,34 +308,11 @@ Engine::~Engine() {
 void Engine::ensure_pinned() {
   if (pinned_[0]) return;
   for (int k = 0; k < kSlots; k++) {
-    ck(cudaHostAlloc(&pinned_[k], kSlotBytes, cudaHostAllocPortable), "cudaHostAlloc");
+    // from the process-wide page-locked pool: a later engine (the next
+    // run) gets the same slots back instead of pinning new memory
+    pinned_[k] = PinnedPool::get().alloc(kSlotBytes);
     ck(cudaEventCreateWithFlags(&slot_ev_[k], cudaEventDisableTiming), "cudaEventCreate");
   }
-}
-
-void Engine::upload(void* dst, const void* src, size_t bytes) {
-  set_device();
-  stats.h2d_bytes += bytes;
-  if (bytes < (1u << 20)) {
-    ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s_), "H2D");
-    sync();
-    return;
-  }
-  ensure_pinned();
-  bool used[kSlots] = {false};
-  size_t off = 0;
-  int k = 0;
-  while (off < bytes) {
-    const size_t n = std::min(kSlotBytes, bytes - off);
-    if (used[k]) ck(cudaEventSynchronize(slot_ev_[k]), "cudaEventSynchronize");
-    copy_parallel(pinned_[k], (const char*)src + off, n);
-    ck(cudaMemcpyAsync((char*)dst + off, pinned_[k], n, cudaMemcpyHostToDevice, s_), "H2D");
-    ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
-    used[k] = true;
-    off += n;
-    k = (k + 1) % kSlots;
-  }
-  sync();
 }
 
 void Engine::download(void* dst, const void* src, size_t bytes) {
@@ -463,7 +440,6 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
     if (index.emplace(v, vs.size()).second) vs.push_back(v);
   }
   if (vs.empty()) return;
-  if (vs.size() == 1) return to_device(*vs[0]);
   set_device();
   // Text and host bytes from pageable memory share one packed image that
   // goes through the pinned slots; text inside page-locked input memory is
@@ -620,7 +596,7 @@ void Engine::to_host_all(const std::vector<DenseValue*>& in) {
     total = align16(total + v->bytes());
   }
   stats.d2h_bytes += direct;
-  download_image(pcs, total);
+  if (!pcs.empty()) download_image(pcs, total);
   sync();
   stats.download_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
@@ -648,42 +624,14 @@ void Engine::to_device(DenseValue& v) {
   if (v.dev && v.dev->device == dev_) return;
   if (v.poison) throw std::runtime_error("a poison value has no bytes");
   set_device();
-  const uint64_t bytes = v.bytes();
-  auto buf = std::make_shared<DeviceBuf>(dev_, bytes);
-  if (!v.host.empty()) {
-    upload(buf->ptr, v.host.data(), bytes);
-  } else if (!v.hex.empty()) {
-    DeviceBuf text(dev_, v.hex.size());
-    upload(text.ptr, v.hex.data(), v.hex.size());
-    if (!aux_) aux_ = std::make_unique<DeviceBuf>(dev_, sizeof(dcf_status));
-    dcf_status* st = (dcf_status*)aux_->ptr;
-    check(dcf_status_reset_async(st, s_), "status reset");
-    check(dcf_hex_decode_async((const char*)text.ptr, v.hex.size(), buf->ptr, st, s_), "hex decode");
-    dcf_status h;
-    ck(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s_), "D2H status");
-    sync();
-    if (h.first_fail != ~0ull) throw std::runtime_error("invalid hex digit in a dense literal");
-  } else if (v.dev) {
-    ck(cudaMemcpyPeerAsync(buf->ptr, dev_, v.dev->ptr, v.dev->device, bytes, s_), "peer copy");
-    sync();
-  } else if (bytes) {
-    throw std::runtime_error("constant has no bytes");
-  }
-  v.dev = buf;
-}
-
-void Engine::to_host(DenseValue& v) {
-  if (!v.host.empty() || v.bytes() == 0) return;
-  if (v.poison) throw std::runtime_error("a poison value has no bytes");
-  if (!v.hex.empty() && v.hex.size() <= kSmallHex) {
-    decode_small(v.hex, v.host);
+  if (v.bytes() == 0) {
+    v.dev = std::make_shared<DeviceBuf>(dev_, 0);
     return;
   }
-  if (!v.dev) to_device(v);
-  set_device();
-  v.host.resize(v.bytes());
-  download(v.host.data(), v.dev->ptr, v.bytes());
+  to_device_all({&v});
 }
+
+void Engine::to_host(DenseValue& v) { to_host_all({&v}); }
 
 uint64_t Engine::bits0_of(DenseValue& v) {
   if (v.host.empty() && !v.hex.empty()) {
@@ -759,8 +707,10 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     to_device_all(ins);
   }
   const auto t1 = std::chrono::steady_clock::now();
-  dcf_status* st = statuses(R);
-  ck(cudaMemsetAsync(st, 0xFF, R * sizeof(dcf_status), s_), "status reset");
+  // Statuses: one per request, and a second block for the second results
+  // of two-result folds.
+  dcf_status* st = statuses(2 * R);
+  ck(cudaMemsetAsync(st, 0xFF, 2 * R * sizeof(dcf_status), s_), "status reset");
 
   // Splat operands: one element each, packed 16-byte aligned and uploaded once.
   std::vector<uint8_t> scal;
@@ -790,7 +740,7 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     return v.dev->ptr;
   };
 
-  std::vector<std::shared_ptr<DeviceBuf>> outs(R);
+  std::vector<std::shared_ptr<DeviceBuf>> outs(R), outs2(R);
   std::vector<const void*> ls(R, nullptr), rs(R, nullptr), cs(R, nullptr);
   for (size_t i = 0; i < R; i++) {
     FoldRequest& q = *reqs[i];
@@ -799,6 +749,7 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     cs[i] = q.cond ? operand(*q.cond, cpos[i]) : nullptr;
     if (q.kind != FoldRequest::SPLAT_SCAN)
       outs[i] = std::make_shared<DeviceBuf>(dev_, q.n * dcf_dtype_size((dcf_dtype)q.out_dtype));
+    if (q.op2) outs2[i] = std::make_shared<DeviceBuf>(dev_, q.n * dcf_dtype_size((dcf_dtype)q.out2_dtype));
   }
   // Many small folds of one kind (one per isolated function, say) go out as
   // one launch per group through the batched kernel.
@@ -809,7 +760,7 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     for (size_t i = 0; i < R; i++) {
       const FoldRequest& q = *reqs[i];
       if ((q.kind == FoldRequest::BINARY || q.kind == FoldRequest::CONVERT || q.kind == FoldRequest::RECIPROCAL) &&
-          q.n <= (4u << 20))
+          q.n <= (4u << 20) && !q.op2)
         groups[{(int)q.kind, q.op, q.dtype, q.out_dtype, q.flags}].push_back(i);
     }
     for (auto& [key, idx] : groups) {
@@ -855,6 +806,10 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
         check(dcf_binary_async((dcf_op)q.op, (dcf_dtype)q.dtype, l, q.lhs->splat, r, q.rhs->splat, q.n, q.flags,
                                outs[i]->ptr, st + i, s_),
               "binary fold");
+        if (q.op2)
+          check(dcf_binary_async((dcf_op)q.op2, (dcf_dtype)q.dtype, l, q.lhs->splat, r, q.rhs->splat, q.n, q.flags2,
+                                 outs2[i]->ptr, st + R + i, s_),
+                "binary fold");
         break;
       case FoldRequest::CONVERT:
         check(dcf_convert_async((dcf_op)q.op, (dcf_dtype)q.dtype, (dcf_dtype)q.out_dtype, l, q.lhs->splat, q.n,
@@ -880,25 +835,53 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
         break;
     }
   }
-  std::vector<dcf_status> hst(R);
-  ck(cudaMemcpyAsync(hst.data(), st, R * sizeof(dcf_status), cudaMemcpyDeviceToHost, s_), "D2H status");
+  std::vector<dcf_status> hst(2 * R);
+  ck(cudaMemcpyAsync(hst.data(), st, 2 * R * sizeof(dcf_status), cudaMemcpyDeviceToHost, s_), "D2H status");
   sync();
   for (size_t i = 0; i < R; i++)
     if (batched[i]) hst[i] = bst[i];
   // First element of every all-equal result, fetched together.
-  std::vector<uint64_t> first(R, 0);
+  std::vector<uint64_t> first(2 * R, 0);
   bool any = false;
   for (size_t i = 0; i < R; i++) {
     FoldRequest& q = *reqs[i];
-    if (hst[i].error != 0xFFFFFFFFu) throw std::runtime_error("a fold kernel gave up waiting for its copies");
+    if (hst[i].error != 0xFFFFFFFFu || (q.op2 && hst[R + i].error != 0xFFFFFFFFu))
+      throw std::runtime_error("a fold kernel gave up waiting for its copies");
     if (q.kind == FoldRequest::SPLAT_SCAN || q.kind == FoldRequest::PERMUTE) continue;
-    if (hst[i].first_fail == ~0ull && hst[i].splat_word != 0) {
-      const size_t oes = dcf_dtype_size((dcf_dtype)q.out_dtype);
-      ck(cudaMemcpyAsync(&first[i], outs[i]->ptr, oes, cudaMemcpyDeviceToHost, s_), "D2H element");
-      any = true;
+    for (size_t k = 0; k < (q.op2 ? 2u : 1u); k++) {
+      const dcf_status& h = hst[k * R + i];
+      if (h.first_fail == ~0ull && h.splat_word != 0) {
+        const size_t oes = dcf_dtype_size((dcf_dtype)(k ? q.out2_dtype : q.out_dtype));
+        ck(cudaMemcpyAsync(&first[k * R + i], (k ? outs2 : outs)[i]->ptr, oes, cudaMemcpyDeviceToHost, s_),
+           "D2H element");
+        any = true;
+      }
     }
   }
   if (any) sync();
+  // A folded result: one element if the kernel saw all values equal (as
+  // MLIR stores a splat), else the device buffer.
+  auto result = [&](const FoldRequest& q, const dcf_status& h, const std::shared_ptr<DeviceBuf>& buf, int dtype,
+                    const TypeP& ty, uint64_t first_bits) {
+    auto d = std::make_shared<DenseValue>();
+    d->ty = ty;
+    d->elements = q.out_elements;
+    d->dtype = dtype;
+    d->es = dcf_dtype_size((dcf_dtype)dtype);
+    if (q.kind != FoldRequest::PERMUTE && h.splat_word != 0) {
+      d->splat = true;
+      d->n = 1;
+      d->host.resize(d->es);
+      memcpy(d->host.data(), &first_bits, d->es);
+    } else {
+      d->n = q.n;
+      d->dev = buf;
+      // The kernel's splat test already said the values differ.
+      if (q.kind != FoldRequest::PERMUTE) d->all_equal = 0;
+    }
+    if (q.kind == FoldRequest::PERMUTE && q.lhs->all_equal == 1) d->all_equal = 1;
+    return d;
+  };
   for (size_t i = 0; i < R; i++) {
     FoldRequest& q = *reqs[i];
     stats.requests++;
@@ -907,26 +890,11 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
       continue;
     }
     q.first_fail = q.kind == FoldRequest::PERMUTE ? ~0ull : hst[i].first_fail;
+    if (q.op2 && hst[R + i].first_fail < q.first_fail) q.first_fail = hst[R + i].first_fail;
     q.folded = q.first_fail == ~0ull;
     if (!q.folded) continue;
-    auto d = std::make_shared<DenseValue>();
-    d->ty = q.out_ty;
-    d->elements = q.out_elements;
-    d->dtype = q.out_dtype;
-    d->es = dcf_dtype_size((dcf_dtype)q.out_dtype);
-    if (q.kind != FoldRequest::PERMUTE && hst[i].splat_word != 0) {
-      d->splat = true;
-      d->n = 1;
-      d->host.resize(d->es);
-      memcpy(d->host.data(), &first[i], d->es);
-    } else {
-      d->n = q.n;
-      d->dev = outs[i];
-      // The kernel's splat test already said the values differ.
-      if (q.kind != FoldRequest::PERMUTE) d->all_equal = 0;
-    }
-    if (q.kind == FoldRequest::PERMUTE && q.lhs->all_equal == 1) d->all_equal = 1;
-    q.out = d;
+    q.out = result(q, hst[i], outs[i], q.out_dtype, q.out_ty, first[i]);
+    if (q.op2) q.out2 = result(q, hst[R + i], outs2[i], q.out2_dtype, q.out2_ty, first[R + i]);
   }
   stats.batches++;
   stats.device_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();

@@ -47,6 +47,12 @@ struct FoldRequest {
   std::vector<int64_t> shape, perms;    // PERMUTE
   TypeP out_ty;                         // attribute type of the result
   bool out_elements = true;
+  // A second result over the same operands (the *_extended ops): a second
+  // binary kernel `op2` writing out2_dtype elements of type out2_ty.
+  int op2 = 0, out2_dtype = 0;
+  uint32_t flags2 = 0;
+  TypeP out2_ty;
+  DenseP out2;
   // outcome
   bool folded = false;
   uint64_t first_fail = ~0ull;
@@ -107,10 +113,9 @@ class Engine {
     pinned_len_ = bytes;
   }
 
-  // Host <-> device copies of `bytes` (synchronous).  Large copies from
-  // pageable memory go through pinned staging slots, filled and emptied by
-  // several host threads while the copy engine moves the previous slot.
-  void upload(void* dst, const void* src, size_t bytes);
+  // Device -> host copy of `bytes` (synchronous).  Large copies to
+  // pageable memory go through pinned staging slots, emptied by several
+  // host threads while the copy engine fills the next slot.
   void download(void* dst, const void* src, size_t bytes);
 
  private:

@@ -146,10 +146,20 @@ DenseP splat_value(TypeP ty, uint64_t bits) {
 // ------------------------------------------------------------- fold plans
 
 struct Plan {
-  enum K { FAILED, INPLACE, VALUE, ATTR, DEVICE } k = FAILED;
+  enum K { FAILED, INPLACE, VALUE, ATTR, DEVICE, MULTI } k = FAILED;
   Value* value = nullptr;
   DenseP attr;
   std::unique_ptr<FoldRequest> req;
+  // MULTI (Fold::Results): one part per result, a value or an attribute.
+  std::vector<std::pair<Value*, DenseP>> parts;
+  static Plan multi(std::vector<std::pair<Value*, DenseP>> ps) {
+    Plan p;
+    for (auto& x : ps)
+      if (!x.first && !x.second) return p;
+    p.k = MULTI;
+    p.parts = std::move(ps);
+    return p;
+  }
   static Plan failed() { return Plan{}; }
   static Plan inplace() {
     Plan p;
@@ -202,8 +212,15 @@ class ArithFolder {
   // ArithFolder::fold, src/patterns/arith/canonicalize.rs:270-491.
   Plan fold() {
     const std::string& name = op_->name;
-    if (name.rfind("arith.", 0) != 0 || op_->results.size() != 1) return Plan::failed();
+    if (name.rfind("arith.", 0) != 0) return Plan::failed();
     const std::string o = name.substr(6);
+    if (op_->results.size() == 2) {  // the *_extended ops (Fold::Results)
+      if (o == "addui_extended") return addui_extended();
+      if (o == "subui_extended") return subui_extended();
+      if (o == "mulsi_extended" || o == "mului_extended") return mul_extended(o == "mulsi_extended");
+      return Plan::failed();
+    }
+    if (op_->results.size() != 1) return Plan::failed();
     uint64_t x;
     if (o == "addi") return addi();
     if (o == "subi") return subi();
@@ -531,6 +548,47 @@ class ArithFolder {
       }
     }
     return float_convert(DCF_TRUNCF);
+  }
+
+  // The second result of a two-result fold: a second kernel over the same
+  // operands, writing `dtype` elements of type `ty`.
+  static Plan with_second(Plan p, int op2, uint32_t flags2, int dtype2, TypeP ty2) {
+    if (p.k == Plan::ATTR) return Plan::multi({{nullptr, p.attr}, {nullptr, p.attr}});  // poison in, poison out
+    if (p.k != Plan::DEVICE) return Plan::failed();
+    p.req->op2 = op2;
+    p.req->flags2 = flags2;
+    p.req->out2_dtype = dtype2;
+    p.req->out2_ty = std::move(ty2);
+    return p;
+  }
+
+  Plan addui_extended() {  // :878-893
+    const TypeP ovt = op_->results[1]->ty;
+    if (zero(1)) return Plan::multi({{v(0), nullptr}, {nullptr, zero_attr(ovt)}});
+    Plan sum = binary(DCF_ADDI, 0, nullptr);
+    if (sum.k != Plan::DEVICE) return with_second(std::move(sum), 0, 0, 0, nullptr);
+    TypeP i1 = with_element(sum.req->out_ty, "i1");
+    return with_second(std::move(sum), DCF_ADDUI_CARRY, 0, DCF_I1, i1);
+  }
+
+  Plan subui_extended() {  // :895-914
+    const TypeP bt = op_->results[1]->ty;
+    if (zero(1)) return Plan::multi({{v(0), nullptr}, {nullptr, zero_attr(bt)}});
+    if (v(0) == v(1)) return Plan::multi({{nullptr, zero_attr(op_->results[0]->ty)}, {nullptr, zero_attr(bt)}});
+    Plan diff = binary(DCF_SUBI, 0, nullptr);
+    if (diff.k != Plan::DEVICE) return with_second(std::move(diff), 0, 0, 0, nullptr);
+    TypeP i1 = with_element(diff.req->out_ty, "i1");
+    return with_second(std::move(diff), DCF_CMPI, DCF_FLAG_PRED(6), DCF_I1, i1);  // borrow: a <u b
+  }
+
+  Plan mul_extended(bool is_signed) {  // :928-949
+    if (zero(1)) return Plan::multi({{nullptr, c_[1]}, {nullptr, c_[1]}});
+    if (!is_signed && one(1)) return Plan::multi({{v(0), nullptr}, {nullptr, zero_attr(v(0)->ty)}});
+    Plan low = binary(DCF_MULI, 0, nullptr);
+    if (low.k != Plan::DEVICE) return with_second(std::move(low), 0, 0, 0, nullptr);
+    TypeP t = low.req->out_ty;
+    const int dt = low.req->out_dtype;
+    return with_second(std::move(low), is_signed ? DCF_MULSI_HI : DCF_MULUI_HI, 0, dt, t);
   }
 
   Plan float_unary(int dop) {
@@ -1029,6 +1087,32 @@ struct Greedy::Impl {
     return own;
   }
 
+  // replace_folded for several results: each part is a value or an
+  // attribute that is materialised as a constant; nothing changes unless
+  // every attribute materialises.
+  bool replace_with_parts(Op* op, const std::vector<std::pair<Value*, DenseP>>& parts) {
+    if (parts.size() != op->results.size()) return false;
+    std::vector<Op*> made;
+    std::vector<Value*> vals;
+    for (size_t i = 0; i < parts.size(); i++) {
+      if (parts[i].first) {
+        vals.push_back(parts[i].first);
+        continue;
+      }
+      Op* c = materialize(m, op->dialect(), parts[i].second, op->results[i]->ty);
+      if (!c) return false;
+      c->loc = op->loc;
+      made.push_back(c);
+      vals.push_back(c->results[0]);
+    }
+    for (Op* c : made) {
+      m.insert_before(c, op);
+      add(c);
+    }
+    replace_op(op, vals);
+    return true;
+  }
+
   // replace_folded (src/rewrite.rs:880-906) for one result.
   bool replace_with_attr(Op* op, const DenseP& a, const std::string& dialect) {
     Op* c = materialize(m, dialect, a, op->results[0]->ty);
@@ -1080,6 +1164,10 @@ struct Greedy::Impl {
           if (req->folded && replace_with_attr(op, req->out, "tosa")) changed = true;
           continue;
         }
+        if (req->folded && req->op2) {
+          if (replace_with_parts(op, {{nullptr, req->out}, {nullptr, req->out2}})) changed = true;
+          continue;
+        }
         if (req->folded && replace_with_attr(op, req->out, op->dialect())) {
           changed = true;
           continue;
@@ -1118,6 +1206,10 @@ struct Greedy::Impl {
           continue;
         }
         if (p.k == Plan::ATTR && replace_with_attr(op, p.attr, op->dialect())) {
+          changed = true;
+          continue;
+        }
+        if (p.k == Plan::MULTI && replace_with_parts(op, p.parts)) {
           changed = true;
           continue;
         }
@@ -1164,48 +1256,57 @@ GreedyConfig config_for(const std::string& pass) {
   throw std::runtime_error("unknown pass `" + pass + "`");
 }
 
-// Run drivers round by round; each round executes every pending request of
-// one engine as one batch (engines in parallel).
+// Run the drivers of each GPU round by round: a round steps every driver
+// until it needs element work and executes all pending requests as one
+// batch.  The GPUs' drivers touch disjoint isolated functions, so each GPU
+// runs its rounds in its own host thread, independent of the others.
 void drive(std::vector<std::unique_ptr<Greedy>>& drivers, std::vector<Engine*>& engines, PassStats* stats) {
-  for (;;) {
-    std::unordered_map<Engine*, std::vector<FoldRequest*>> reqs;
-    bool any = false;
-    for (auto& d : drivers) {
-      if (d->done()) continue;
-      FoldRequest* r = d->step();
-      if (r) {
-        reqs[&d->engine()].push_back(r);
-        any = true;
-      }
-    }
-    if (!any) return;
-    if (reqs.size() == 1) {
-      reqs.begin()->first->execute(reqs.begin()->second);
-    } else {
-      std::vector<std::thread> th;
-      std::vector<std::string> errs(reqs.size());
-      size_t i = 0;
-      for (auto& kv : reqs) {
-        th.emplace_back([&, i, e = kv.first, rs = &kv.second] {
-          try {
-            e->execute(*rs);
-          } catch (const std::exception& ex) {
-            errs[i] = ex.what();
-          }
-        });
-        i++;
-      }
-      for (auto& t : th) t.join();
-      for (auto& e : errs)
-        if (!e.empty()) throw std::runtime_error(e);
-    }
-    if (stats)
-      for (auto& kv : reqs)
-        for (FoldRequest* r : kv.second) {
-          if (r->folded) stats->folds++;
-          else stats->refused++;
-        }
+  (void)engines;
+  std::vector<Engine*> order;
+  std::unordered_map<Engine*, std::vector<Greedy*>> per;
+  for (auto& d : drivers) {
+    if (!per.count(&d->engine())) order.push_back(&d->engine());
+    per[&d->engine()].push_back(d.get());
   }
+  std::vector<PassStats> local(order.size());
+  auto rounds = [&](size_t k) {
+    Engine* e = order[k];
+    for (;;) {
+      std::vector<FoldRequest*> reqs;
+      for (Greedy* d : per[e]) {
+        if (d->done()) continue;
+        if (FoldRequest* r = d->step()) reqs.push_back(r);
+      }
+      if (reqs.empty()) return;
+      e->execute(reqs);
+      for (FoldRequest* r : reqs) {
+        if (r->folded) local[k].folds++;
+        else local[k].refused++;
+      }
+    }
+  };
+  if (order.size() == 1) {
+    rounds(0);
+  } else {
+    std::vector<std::thread> th;
+    std::vector<std::string> errs(order.size());
+    for (size_t k = 0; k < order.size(); k++)
+      th.emplace_back([&, k] {
+        try {
+          rounds(k);
+        } catch (const std::exception& ex) {
+          errs[k] = ex.what();
+        }
+      });
+    for (auto& t : th) t.join();
+    for (auto& e : errs)
+      if (!e.empty()) throw std::runtime_error(e);
+  }
+  if (stats)
+    for (const PassStats& p : local) {
+      stats->folds += p.folds;
+      stats->refused += p.refused;
+    }
 }
 
 uint64_t constant_bytes(Op* op) {

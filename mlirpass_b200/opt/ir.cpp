@@ -133,23 +133,27 @@ void Op::set_prop(const std::string& key, const std::string& text) {
 }
 
 Op* Module::new_op(const std::string& name) {
+  std::lock_guard<std::mutex> g(mu_);
   ops_.push_back(std::make_unique<Op>());
   ops_.back()->name = name;
   return ops_.back().get();
 }
 
 Value* Module::new_value(TypeP ty) {
+  std::lock_guard<std::mutex> g(mu_);
   values_.push_back(std::make_unique<Value>());
   values_.back()->ty = std::move(ty);
   return values_.back().get();
 }
 
 Block* Module::new_block() {
+  std::lock_guard<std::mutex> g(mu_);
   blocks_.push_back(std::make_unique<Block>());
   return blocks_.back().get();
 }
 
 Region* Module::new_region() {
+  std::lock_guard<std::mutex> g(mu_);
   regions_.push_back(std::make_unique<Region>());
   return regions_.back().get();
 }

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <list>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <string_view>
 #include <unordered_map>
@@ -185,6 +186,9 @@ class Module {
   void replace_all_uses(Value* from, Value* to);
 
  private:
+  // Isolated functions are rewritten by one thread per GPU at once: the
+  // node arenas are the only state they share.
+  std::mutex mu_;
   std::vector<std::unique_ptr<Op>> ops_;
   std::vector<std::unique_ptr<Value>> values_;
   std::vector<std::unique_ptr<Block>> blocks_;

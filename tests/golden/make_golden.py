@@ -41,7 +41,8 @@ BINARY_I = {"addi", "subi", "muli", "andi", "ori", "xori", "shli", "shrui", "shr
 CONVERT = {"extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "convertf", "negf", "flush_denormals",
            "extsi", "extui", "trunci", "index_cast", "index_castui", "bitcast"}
 CMP = {"cmpi", "cmpf"}
-ARITH = BINARY_F | BINARY_I | CONVERT | CMP | {"select"}
+EXTENDED = {"addui_extended", "subui_extended", "mulsi_extended", "mului_extended"}
+ARITH = BINARY_F | BINARY_I | CONVERT | CMP | {"select"} | EXTENDED
 TOSA = {"reciprocal", "transpose"}
 
 ALLOWED_FLAGS = ("-split-input-file", "--split-input-file", "-allow-unregistered-dialect",
@@ -129,6 +130,15 @@ def shortcut(op: str, ops, consts, props) -> str | None:
                 return "value0"
             if op.endswith("numf") and f_is(r, dt, "nan"):
                 return "value0"
+    if op in EXTENDED:
+        zero = r is not None and r == 0
+        if zero:
+            return "zero_rhs"
+        if op == "mului_extended" and r == 1:
+            return "one_rhs"
+        if op == "subui_extended" and same:
+            return "same"
+        return None
     if op == "select":
         t_same = ops[1].result == ops[2].result
         c = scalar_of(consts[0])
@@ -222,7 +232,10 @@ def main():
                     consts = [c.const for c in opnds]
                     if any(ambiguous(c) for c in consts):
                         continue
-                    res_ty = parse_type(op.out_types[0]) if len(op.out_types) == 1 else None
+                    k = f.index.get(v, 0)
+                    if len(op.out_types) != op.nres or k >= len(op.out_types):
+                        continue
+                    res_ty = parse_type(op.out_types[k])
                     if res_ty is None:
                         continue
                     gv = g.ret.operands[pos]
@@ -246,6 +259,7 @@ def main():
                             "kind": c.ty.kind, "splat": c.splat, "elements": c.elements,
                             "bits": [format(x, "x") for x in c.bits]} for o, c in zip(opnds, consts)],
                         "result": {"dtype": res_ty.elem, "shape": res_ty.shape, "kind": res_ty.kind},
+                        "result_index": k, "result_types": op.out_types,
                         "shortcut": shortcut(short, opnds, consts, props) if dialect == "arith" else None,
                         "expected": exp,
                     }

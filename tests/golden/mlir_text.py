@@ -194,7 +194,7 @@ def parse_const(lit: str, ty: Ty) -> ConstVal | None:
         return None
 
 
-_OP = re.compile(r'^\s*(?:(%[\w.$-]+)\s*=\s*)?"([\w.]+)"\((.*?)\)\s*(.*)$')
+_OP = re.compile(r'^\s*(?:(%[\w.$-]+(?::\d+)?)\s*=\s*)?"([\w.]+)"\((.*?)\)\s*(.*)$')
 
 
 @dataclass
@@ -208,6 +208,7 @@ class Op:
     line: str
     const: ConstVal | None = None
     prop_map: dict = field(default_factory=dict)
+    nres: int = 1                  # results (an op printed as %name:N has N)
 
 
 def _split_sig(rest: str):
@@ -269,13 +270,15 @@ def parse_op(line: str) -> Op | None:
     if not m:
         return None
     res, name, operands, rest = m.groups()
+    nres = 1
     if res and ":" in res:
-        return None
+        res, k = res.split(":")
+        nres = int(k)
     props, ins, outs = _split_sig(rest.strip())
     if ins is None:
         return None
     ops = [o.strip() for o in operands.split(",") if o.strip()]
-    op = Op(res, name, ops, props, ins, outs, line, prop_map=parse_props(props))
+    op = Op(res, name, ops, props, ins, outs, line, prop_map=parse_props(props), nres=nres)
     if name in ("arith.constant", "tosa.const"):
         key = "value" if name == "arith.constant" else "values"
         v = op.prop_map.get(key)
@@ -291,8 +294,9 @@ def parse_op(line: str) -> Op | None:
 class Func:
     name: str
     ops: list[Op]
-    defs: dict
+    defs: dict                     # value name -> defining op
     ret: Op | None
+    index: dict = field(default_factory=dict)   # value name -> result number (for %name#k)
 
 
 _FUNC = re.compile(r'"func\.func"\(\) <\{.*sym_name = "([^"]+)"')
@@ -314,8 +318,12 @@ def parse_funcs(text: str) -> dict[str, Func]:
         if op is None:
             continue
         cur.ops.append(op)
-        if op.result:
+        if op.result and op.nres == 1:
             cur.defs[op.result] = op
+        elif op.result:
+            for k in range(op.nres):
+                cur.defs[f"{op.result}#{k}"] = op
+                cur.index[f"{op.result}#{k}"] = k
         if op.name == "func.return":
             cur.ret = op
     return funcs

@@ -22,6 +22,7 @@ STORAGE = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
 SIZE = {"i1": 1, "i8": 1, "i16": 2, "i32": 4, "i64": 8, "index": 8, "f16": 2, "bf16": 2, "f32": 4, "f64": 8,
         "f8E5M2": 1, "f8E4M3": 1, "f8E3M4": 1}
 CANON = {"index": "i64"}
+EXTENDED = ("addui_extended", "subui_extended", "mulsi_extended", "mului_extended")
 UNARY = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "convertf", "negf", "flush_denormals", "extsi",
          "extui", "trunci", "index_cast", "index_castui")
 
@@ -97,6 +98,24 @@ def run_case(c, eng):
         f = eng.select(cnd, t, fv, n=n, cond_splat=ops[0]["splat"], t_splat=ops[1]["splat"],
                        f_splat=ops[2]["splat"])
         return "folded", (False, [int(x) for x in f.out[:n]])
+    if op in EXTENDED:
+        # Two results over the same operands (:878-949): result 0 is the
+        # wrapped sum / difference / product, result 1 the carry, the borrow
+        # (a <u b) or the high product half.
+        k = c.get("result_index", 0)
+        (a, dt), (b, dt2) = _arr(ops[0]), _arr(ops[1])
+        if dt != dt2 or ops[0]["elements"] != ops[1]["elements"]:
+            return "not_folded", None
+        ls, rs = ops[0]["splat"], ops[1]["splat"]
+        n = 1 if (ls and rs) else max(len(a), len(b))
+        base = {"addui_extended": "addi", "subui_extended": "subi"}.get(op, "muli")
+        second = {"addui_extended": ("addui_carry", 0), "subui_extended": ("cmpi", 6 << 8),
+                  "mulsi_extended": ("mulsi_hi", 0), "mului_extended": ("mului_hi", 0)}[op]
+        eop, fl = (base, 0) if k == 0 else second
+        f = eng.binary(eop, dt, a, b, n=n, lhs_splat=ls, rhs_splat=rs, flags=fl)
+        if not f.folded:
+            return "not_folded", None
+        return "folded", (ls and rs, [int(x) for x in f.out[:n]])
     # binary
     (a, dt), (b, dt2) = _arr(ops[0]), _arr(ops[1])
     if dt != dt2 or ops[0]["elements"] != ops[1]["elements"] or ops[0]["shape"] != ops[1]["shape"]:

@@ -62,10 +62,17 @@ def render(c):
     args = ", ".join(names)
     if c["op"] == "tosa.transpose":
         args, ins = names[0], ty_text(c["operands"][0])
-    lines.append(f'    %r = "{c["op"]}"({args}){" <{" + p + "}>" if p else ""} : ({ins}) -> {rty}')
+    pr = " <{" + p + "}>" if p else ""
+    all_ty = c.get("result_types") or [rty]
+    if len(all_ty) > 1:   # a two-result op: %r:2 = ..., returning %r#k
+        lines.append(f'    %r:{len(all_ty)} = "{c["op"]}"({args}){pr} : ({ins}) -> ({", ".join(all_ty)})')
+        ret = f'%r#{c["result_index"]}'
+    else:
+        lines.append(f'    %r = "{c["op"]}"({args}){pr} : ({ins}) -> {rty}')
+        ret = "%r"
     return ('"builtin.module"() ({\n'
             f'  "func.func"() <{{function_type = () -> {rty}, sym_name = "t"}}> ({{\n' + "\n".join(lines) +
-            f'\n    "func.return"(%r) : ({rty}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
+            f'\n    "func.return"({ret}) : ({rty}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
 
 
 @pytest.mark.parametrize("case", CASES, ids=[case_id(c) for c in CASES])

@@ -205,3 +205,15 @@ def test_big_list_literals_are_constants():
                       f'    %1 = "arith.bitcast"(%0) : (tensor<{n}xi32>) -> tensor<{n}xf32>'])
     f, d = returned(run(module(body, "%1", f"tensor<{n}xf32>")))
     assert d.name == "arith.constant" and d.const.bits == list(range(n))
+
+
+def test_output_as_array_without_copy():
+    body = const("%0", C4, T)
+    text = module(body, "%0", T)
+    a, st = opt.run(text, "canonicalize", n_gpus=0, as_array=True)
+    view = a[5:]
+    del a
+    import gc
+    gc.collect()
+    assert bytes(view) == opt.run(text, "canonicalize", n_gpus=0, as_bytes=True)[0][5:]
+    assert st["call_ms"] > 0
