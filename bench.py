@@ -485,10 +485,11 @@ def run_kernels(args):
            reps=5)
     w = T(W.config5_weight().view(np.int16))
     wo = torch.empty_like(w)
+    kind = "bulk-tensor pipeline" if os.environ.get("DCF_TRANSPOSE") == "tma" else "tiled loads, prefetched"
     timeit(lambda: dcf.permute_async(2, (16384, 16384), (1, 0), w, wo, st), 4 * w.numel(),
-           ("config5 16384x16384 bf16", "transpose (bulk-tensor pipeline)"))
+           ("config5 16384x16384 bf16", f"transpose (dcf_permute_status_async: {kind})"))
     timeit(lambda: dcf.transpose2d_async(2, 16384, 16384, w, wo), 4 * w.numel(),
-           ("config5 16384x16384 bf16", "transpose (plain loads)"))
+           ("config5 16384x16384 bf16", "transpose (dcf_transpose2d_async: tiled loads, prefetched)"))
 
 
 def run_profile_kernels(args):

@@ -389,6 +389,23 @@ int dcf_hex_decode_many_async(const dcf_hex_piece* pieces, size_t n,
                               uint64_t max_nchars, dcf_status* status,
                               void* stream);
 
+/* One byte range of a batched hash (device pointer). */
+typedef struct dcf_hash_piece {
+  const void* data;
+  uint64_t nbytes;
+} dcf_hash_piece;
+
+/* 64-bit hashes of n device byte ranges with one launch (per 65535):
+ * out[i] (device) gets the hash of pieces[i] (a DEVICE array); max_bytes
+ * bounds every piece's length.  Equal bytes give equal hashes; a caller
+ * that deduplicates constants confirms equal hashes byte for byte.  The
+ * hash is the sum over 8-byte words w_i (the last zero-padded) of
+ * mix(w_i ^ i * 0x9E3779B97F4A7C15) plus mix(nbytes), mix being the
+ * SplitMix64 finaliser.  Stands in for the O(bytes) Attribute equality of
+ * the greedy driver's constant folder (src/rewrite.rs:689-728). */
+int dcf_hash_many_async(const dcf_hash_piece* pieces, size_t n,
+                        uint64_t max_bytes, uint64_t* out, void* stream);
+
 /* Read a device dcf_status back into a dcf_result (synchronises stream). */
 int dcf_status_read(const dcf_status* status, void* stream, dcf_result* res);
 

@@ -120,6 +120,7 @@ SIGNATURES = {
     "dcf_hex_encode_async": (_I, [_VP, _U64, _VP, _VP]),
     "dcf_hex_decode_async": (_I, [_VP, _U64, _VP, _VP, _VP]),
     "dcf_hex_decode_many_async": (_I, [_VP, _SZ, _U64, _VP, _VP]),
+    "dcf_hash_many_async": (_I, [_VP, _SZ, _U64, _VP, _VP]),
     "dcf_status_read": (_I, [_VP, _VP, _RP]),
 }
 

@@ -83,6 +83,8 @@ int launch_hex_encode(const void* in, uint64_t nbytes, char* out, cudaStream_t s
 int launch_hex_decode(const char* in, uint64_t nchars, void* out, dcf_status* st, cudaStream_t stream);
 int launch_hex_decode_pieces(const dcf_hex_piece* pieces, size_t n, uint64_t max_nchars, dcf_status* st,
                              cudaStream_t stream);
+int launch_hash_pieces(const dcf_hash_piece* pieces, size_t n, uint64_t max_bytes, uint64_t* out,
+                       cudaStream_t stream);
 int launch_select(size_t elem_size, const void* cond, int cond_splat, const void* t, int t_splat, const void* f,
                   int f_splat, uint64_t n, void* out, dcf_status* st, cudaStream_t stream);
 int launch_splat_check(const void* in, size_t elem_size, uint64_t n, dcf_status* st, cudaStream_t stream);

@@ -5,6 +5,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 
 #include "dcf_kernels.cuh"
@@ -66,6 +67,17 @@ int tma_min_tiles_per_sm() {
   return v;
 }
 
+// Which 2-byte transpose the status-reporting entry points use: the
+// bulk-tensor pipeline (DCF_TRANSPOSE=tma) or the plain-load kernel with a
+// register prefetch of the next tile (the default: faster on B200).
+bool transpose_tma_enabled() {
+  static const bool v = [] {
+    const char* e = getenv("DCF_TRANSPOSE");
+    return e && std::string(e) == "tma";
+  }();
+  return v;
+}
+
 int sm_count_current() {
   static int sms[64] = {0};
   int dev = 0;
@@ -108,7 +120,21 @@ int launch_ew(const EwLaunch& a) {
 // as 32-bit column pairs of two adjacent rows, 2x2-transposed in registers,
 // and written to an XOR-swizzled 64x32-word shared tile, so that both the
 // global reads and the global writes are 128-byte coalesced rows and the
-// shared-memory accesses are free of bank conflicts.
+// shared-memory accesses are free of bank conflicts.  The next tile's loads
+// are issued before this tile's stores, so they are in flight meanwhile.
+__device__ __forceinline__ void load_tile_b16(const uint32_t* __restrict__ in, uint64_t t, uint64_t tiles_c,
+                                              uint64_t in_words, int warp, int lane, uint32_t (&a)[4],
+                                              uint32_t (&b)[4]) {
+  const uint64_t r0 = (t / tiles_c) * 64, c0 = (t % tiles_c) * 64;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int y = warp + 8 * k;
+    const uint64_t row = r0 + 2 * y;
+    a[k] = __ldg(in + row * in_words + c0 / 2 + lane);
+    b[k] = __ldg(in + (row + 1) * in_words + c0 / 2 + lane);
+  }
+}
+
 __global__ void __launch_bounds__(256) transpose_b16_kernel(const uint32_t* __restrict__ in,
                                                             uint32_t* __restrict__ out, uint64_t rows,
                                                             uint64_t cols) {
@@ -116,16 +142,10 @@ __global__ void __launch_bounds__(256) transpose_b16_kernel(const uint32_t* __re
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t tiles_c = cols / 64, ntiles = (rows / 64) * tiles_c;
   const uint64_t in_words = cols / 2, out_words = rows / 2;
+  uint32_t a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
+  if (blockIdx.x < ntiles) load_tile_b16(in, blockIdx.x, tiles_c, in_words, warp, lane, a, b);
   for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
     const uint64_t r0 = (t / tiles_c) * 64, c0 = (t % tiles_c) * 64;
-    uint32_t a[4], b[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int y = warp + 8 * k;
-      const uint64_t row = r0 + 2 * y;
-      a[k] = __ldg(in + row * in_words + c0 / 2 + lane);
-      b[k] = __ldg(in + (row + 1) * in_words + c0 / 2 + lane);
-    }
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const int y = warp + 8 * k;
@@ -134,6 +154,8 @@ __global__ void __launch_bounds__(256) transpose_b16_kernel(const uint32_t* __re
       s[2 * lane][y ^ lane] = w0;
       s[2 * lane + 1][y ^ lane] = w1;
     }
+    const uint64_t tn = t + gridDim.x;
+    if (tn < ntiles) load_tile_b16(in, tn, tiles_c, in_words, warp, lane, a, b);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < 8; k++) {
@@ -178,14 +200,15 @@ static int sm_count() {
 int launch_transpose2d(size_t es, uint64_t rows, uint64_t cols, const void* in, void* out, cudaStream_t st,
                        dcf_status* status) {
   if (rows == 0 || cols == 0) return DCF_OK;
-  if (es == 2 && status) {
+  if (es == 2 && status && transpose_tma_enabled()) {
     const int rc = launch_transpose2_tma(in, out, rows, cols, status, st);
     if (rc != DCF_EUNSUPPORTED) return rc;
   }
   const int sms = sm_count();
   if (es == 2 && rows % 64 == 0 && cols % 64 == 0 && ((uintptr_t)in & 3) == 0 && ((uintptr_t)out & 3) == 0) {
+    // one wave of persistent CTAs (as many as are resident at once)
     const uint64_t nt = (rows / 64) * (cols / 64);
-    const uint64_t g = nt < (uint64_t)sms * 8 ? nt : (uint64_t)sms * 8;
+    const int g = grid_for(nt * (uint64_t)kThreads * kUnroll, (const void*)transpose_b16_kernel);
     note_launch();
     transpose_b16_kernel<<<(unsigned)g, 256, 0, st>>>((const uint32_t*)in, (uint32_t*)out, rows, cols);
   } else {
@@ -467,11 +490,68 @@ int launch_hex_decode_pieces(const dcf_hex_piece* pieces, size_t n, uint64_t max
   // Blocks per piece: enough for the longest, at most 64; pieces go along y
   // in launches of at most 65535.
   const uint64_t vecs = max_nchars / 16 + 1;
-  const unsigned gx = (unsigned)std::min<uint64_t>(64, (vecs + 4 * 256 - 1) / (4 * 256));
+  const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(4096, (vecs + 4 * 256 - 1) / (4 * 256)));
   for (size_t at = 0; at < n; at += 65535) {
     const unsigned gy = (unsigned)std::min<size_t>(65535, n - at);
     note_launch();
     hex_decode_pieces_kernel<<<dim3(gx, gy), 256, 0, s>>>(pieces + at, st);
+    if (cudaPeekAtLastError() != cudaSuccess) return DCF_ECUDA;
+  }
+  return DCF_OK;
+}
+
+// ------------------------------------------------------------ byte hash
+
+// A 64-bit hash of a byte range for constant deduplication: the sum over
+// its 8-byte words (the last one zero-padded) of mix(word ^ index * phi),
+// plus mix(length).  A sum of independent mixes reduces in any order, so
+// every thread, warp and block adds its part with one atomicAdd.  mix is
+// the SplitMix64 finaliser.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void __launch_bounds__(256) hash_pieces_kernel(const dcf_hash_piece* __restrict__ pieces,
+                                                          unsigned long long* __restrict__ out) {
+  const dcf_hash_piece pc = pieces[blockIdx.y];
+  const uint64_t nw = pc.nbytes / 8, stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint8_t* b = (const uint8_t*)pc.data;
+  const bool aligned = ((uintptr_t)b & 7) == 0;
+  uint64_t h = 0;
+  for (uint64_t i = tid; i < nw; i += stride) {
+    uint64_t w;
+    if (aligned) {
+      w = __ldg((const unsigned long long*)b + i);
+    } else {
+      w = 0;
+      for (int k = 0; k < 8; k++) w |= (uint64_t)b[8 * i + k] << (8 * k);
+    }
+    h += mix64(w ^ (i * 0x9E3779B97F4A7C15ull));
+  }
+  if (tid == 0) {
+    uint64_t w = 0;
+    for (uint64_t k = nw * 8; k < pc.nbytes; k++) w |= (uint64_t)b[k] << (8 * (k - nw * 8));
+    if (pc.nbytes % 8) h += mix64(w ^ (nw * 0x9E3779B97F4A7C15ull));
+    h += mix64(pc.nbytes);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) h += __shfl_xor_sync(0xFFFFFFFFu, h, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(out + blockIdx.y, (unsigned long long)h);
+}
+
+int launch_hash_pieces(const dcf_hash_piece* pieces, size_t n, uint64_t max_bytes, uint64_t* out, cudaStream_t s) {
+  if (n == 0) return DCF_OK;
+  if (cudaMemsetAsync(out, 0, n * sizeof(uint64_t), s) != cudaSuccess) return DCF_ECUDA;
+  // about 16 words per thread on the longest piece
+  const uint64_t words = max_bytes / 8 + 1;
+  const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(4096, (words + 16 * 256 - 1) / (16 * 256)));
+  for (size_t at = 0; at < n; at += 65535) {
+    const unsigned gy = (unsigned)std::min<size_t>(65535, n - at);
+    note_launch();
+    hash_pieces_kernel<<<dim3(gx, gy), 256, 0, s>>>(pieces + at, (unsigned long long*)out + at);
     if (cudaPeekAtLastError() != cudaSuccess) return DCF_ECUDA;
   }
   return DCF_OK;

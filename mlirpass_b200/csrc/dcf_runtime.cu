@@ -1137,6 +1137,16 @@ int dcf_hex_decode_many_async(const dcf_hex_piece* pieces, size_t n, uint64_t ma
   return DCF_OK;
 }
 
+int dcf_hash_many_async(const dcf_hash_piece* pieces, size_t n, uint64_t max_bytes, uint64_t* out, void* stream) {
+  if (n == 0) return DCF_OK;
+  if (!pieces || !out) return set_err(DCF_EINVAL, "null pointer");
+  int rc = select_device(out);
+  if (rc) return rc;
+  rc = launch_hash_pieces(pieces, n, max_bytes, out, (cudaStream_t)stream);
+  if (rc) return set_err(rc, "hash launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return DCF_OK;
+}
+
 int dcf_status_read(const dcf_status* status, void* stream, dcf_result* res) {
   if (!status || !res) return set_err(DCF_EINVAL, "null pointer");
   if (int rc = select_device(status)) return rc;

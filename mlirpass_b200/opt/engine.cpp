@@ -533,33 +533,89 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
   // into pieces of at most kPieceChars characters so the grid stays even.
   constexpr uint64_t kPieceChars = 4u << 20;
   std::vector<dcf_hex_piece> pieces;
-  uint64_t max_chars = 0;
   for (const Loc& l : text) {
     const uint64_t nchars = l.v->hex.size();
     for (uint64_t c = 0; c < nchars; c += kPieceChars) {
       const uint64_t len = std::min<uint64_t>(kPieceChars, nchars - c);
       pieces.push_back({at(l) + c, (char*)buf_of(l.v)->ptr + c / 2, len});
-      max_chars = std::max(max_chars, len);
     }
   }
   std::unique_ptr<DeviceBuf> pdesc;
   if (!pieces.empty()) {
+    // pieces of similar length together, one launch per length class
+    std::stable_sort(pieces.begin(), pieces.end(),
+                     [](const dcf_hex_piece& x, const dcf_hex_piece& y) { return x.nchars < y.nchars; });
     pdesc = std::make_unique<DeviceBuf>(dev_, pieces.size() * sizeof(dcf_hex_piece));
     ck(cudaMemcpyAsync(pdesc->ptr, pieces.data(), pieces.size() * sizeof(dcf_hex_piece), cudaMemcpyHostToDevice, s_),
        "H2D pieces");
-    check(dcf_hex_decode_many_async((const dcf_hex_piece*)pdesc->ptr, pieces.size(), max_chars, st, s_),
-          "hex decode");
+    auto cls = [](uint64_t n) { return n ? 64 - __builtin_clzll(n) : 0; };
+    for (size_t a = 0; a < pieces.size();) {
+      size_t b = a + 1;
+      while (b < pieces.size() && cls(pieces[b].nchars) == cls(pieces[a].nchars)) b++;
+      check(dcf_hex_decode_many_async((const dcf_hex_piece*)pdesc->ptr + a, b - a, pieces[b - 1].nchars, st, s_),
+            "hex decode");
+      a = b;
+    }
   }
   for (const Loc& l : raw)
     ck(cudaMemcpyAsync(buf_of(l.v)->ptr, at(l), l.v->bytes(), cudaMemcpyDeviceToDevice, s_), "D2D");
   for (DenseValue* v : vs)
     if (v->host.empty() && v->hex.empty())
       ck(cudaMemcpyPeerAsync(buf_of(v)->ptr, dev_, v->dev->ptr, v->dev->device, v->bytes(), s_), "peer copy");
+  // Hashes of the new device copies (constant deduplication compares
+  // hashes first), read back with the decode status.
+  std::vector<uint64_t> hashes(vs.size(), 0);
+  std::unique_ptr<DeviceBuf> hdesc, hout;
+  hash_async(bufs, vs, hdesc, hout);
   dcf_status h;
   ck(cudaMemcpyAsync(&h, st, sizeof h, cudaMemcpyDeviceToHost, s_), "D2H status");
+  if (hout) ck(cudaMemcpyAsync(hashes.data(), hout->ptr, vs.size() * 8, cudaMemcpyDeviceToHost, s_), "D2H hashes");
   sync();
   if (h.first_fail != ~0ull) throw std::runtime_error("invalid hex digit in a dense literal");
-  for (size_t i = 0; i < vs.size(); i++) vs[i]->dev = bufs[i];
+  for (size_t i = 0; i < vs.size(); i++) {
+    vs[i]->dev = bufs[i];
+    if (hout) {
+      vs[i]->hash = hashes[i];
+      vs[i]->hashed = true;
+    }
+  }
+}
+
+// Queue dcf_hash_many_async over device buffers (sizes from the values).
+void Engine::hash_async(const std::vector<std::shared_ptr<DeviceBuf>>& bufs, const std::vector<DenseValue*>& vs,
+                        std::unique_ptr<DeviceBuf>& desc, std::unique_ptr<DeviceBuf>& out) {
+  std::vector<dcf_hash_piece> pcs(bufs.size());
+  for (size_t i = 0; i < bufs.size(); i++) pcs[i] = {bufs[i] ? bufs[i]->ptr : nullptr, bufs[i] ? vs[i]->bytes() : 0};
+  if (pcs.empty()) return;
+  desc = std::make_unique<DeviceBuf>(dev_, pcs.size() * sizeof(dcf_hash_piece));
+  out = std::make_unique<DeviceBuf>(dev_, pcs.size() * sizeof(uint64_t));
+  ck(cudaMemcpyAsync(desc->ptr, pcs.data(), pcs.size() * sizeof(dcf_hash_piece), cudaMemcpyHostToDevice, s_),
+     "H2D hash pieces");
+  // The grid follows the longest piece of a launch: pieces within a factor
+  // of two of each other's length go in one launch (runs of the given
+  // order), so a few long pieces do not widen the grid of many short ones.
+  auto cls = [](uint64_t n) { return n ? 64 - __builtin_clzll(n) : 0; };
+  for (size_t a = 0; a < pcs.size();) {
+    size_t b = a + 1;
+    uint64_t maxb = pcs[a].nbytes;
+    while (b < pcs.size() && cls(pcs[b].nbytes) == cls(pcs[a].nbytes)) maxb = std::max(maxb, pcs[b++].nbytes);
+    check(dcf_hash_many_async((const dcf_hash_piece*)desc->ptr + a, b - a, maxb, (uint64_t*)out->ptr + a, s_),
+          "hash");
+    a = b;
+  }
+}
+
+uint64_t Engine::hash_of(DenseValue& v) {
+  if (v.hashed) return v.hash;
+  to_device(v);  // hashes it when it uploads
+  if (!v.hashed) {
+    std::unique_ptr<DeviceBuf> d, o;
+    hash_async({v.dev}, {&v}, d, o);
+    ck(cudaMemcpyAsync(&v.hash, o->ptr, 8, cudaMemcpyDeviceToHost, s_), "D2H hash");
+    sync();
+    v.hashed = true;
+  }
+  return v.hash;
 }
 
 void Engine::to_host_all(const std::vector<DenseValue*>& in) {
@@ -835,8 +891,32 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
         break;
     }
   }
+  // Hashes of every result (used by constant deduplication), read back
+  // with the statuses.
+  std::vector<uint64_t> rh(2 * R, 0);
+  std::unique_ptr<DeviceBuf> hdesc, hout;
+  {
+    std::vector<std::shared_ptr<DeviceBuf>> hb(2 * R);
+    std::vector<DenseValue> sizes(2 * R);
+    std::vector<DenseValue*> sv(2 * R);
+    for (size_t i = 0; i < R; i++) {
+      const FoldRequest& q = *reqs[i];
+      if (q.kind == FoldRequest::SPLAT_SCAN) continue;
+      hb[i] = outs[i];
+      sizes[i].n = q.n;
+      sizes[i].es = dcf_dtype_size((dcf_dtype)q.out_dtype);
+      if (q.op2) {
+        hb[R + i] = outs2[i];
+        sizes[R + i].n = q.n;
+        sizes[R + i].es = dcf_dtype_size((dcf_dtype)q.out2_dtype);
+      }
+    }
+    for (size_t i = 0; i < 2 * R; i++) sv[i] = &sizes[i];
+    hash_async(hb, sv, hdesc, hout);
+  }
   std::vector<dcf_status> hst(2 * R);
   ck(cudaMemcpyAsync(hst.data(), st, 2 * R * sizeof(dcf_status), cudaMemcpyDeviceToHost, s_), "D2H status");
+  if (hout) ck(cudaMemcpyAsync(rh.data(), hout->ptr, 2 * R * 8, cudaMemcpyDeviceToHost, s_), "D2H hashes");
   sync();
   for (size_t i = 0; i < R; i++)
     if (batched[i]) hst[i] = bst[i];
@@ -894,7 +974,17 @@ void Engine::execute(const std::vector<FoldRequest*>& reqs) {
     q.folded = q.first_fail == ~0ull;
     if (!q.folded) continue;
     q.out = result(q, hst[i], outs[i], q.out_dtype, q.out_ty, first[i]);
-    if (q.op2) q.out2 = result(q, hst[R + i], outs2[i], q.out2_dtype, q.out2_ty, first[R + i]);
+    if (q.out->dev) {
+      q.out->hash = rh[i];
+      q.out->hashed = true;
+    }
+    if (q.op2) {
+      q.out2 = result(q, hst[R + i], outs2[i], q.out2_dtype, q.out2_ty, first[R + i]);
+      if (q.out2->dev) {
+        q.out2->hash = rh[R + i];
+        q.out2->hashed = true;
+      }
+    }
   }
   stats.batches++;
   stats.device_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();

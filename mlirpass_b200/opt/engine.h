@@ -101,6 +101,9 @@ class Engine {
   // the value is there).
   std::string hex_of(DenseValue& v);
   uint64_t bits0_of(DenseValue& v);
+  // 64-bit hash of the bytes (dcf_hash_many_async; computed on upload and
+  // for every fold result, so deduplication rarely launches anything).
+  uint64_t hash_of(DenseValue& v);
   // Whether every value equals the first (cached in v.all_equal).
   bool all_equal(DenseValue& v);
 
@@ -134,6 +137,8 @@ class Engine {
   void* pinned_[kSlots] = {nullptr};
   cudaEvent_t slot_ev_[kSlots] = {nullptr};
   void ensure_pinned();
+  void hash_async(const std::vector<std::shared_ptr<DeviceBuf>>& bufs, const std::vector<DenseValue*>& vs,
+                  std::unique_ptr<DeviceBuf>& desc, std::unique_ptr<DeviceBuf>& out);
   void upload_image(const std::vector<ImagePiece>& pcs, size_t total, char* arena);
   void download_image(const std::vector<ImagePiece>& pcs, size_t total);
   void run_batched(const std::vector<FoldRequest*>& reqs, const std::vector<const void*>& ls,

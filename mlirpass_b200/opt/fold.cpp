@@ -871,13 +871,32 @@ Op* materialize(Module& m, const std::string& dialect, const DenseP& value, cons
   return nullptr;
 }
 
-bool value_eq(const DenseP& a, const DenseP& b) {
+// Attribute equality of two constants (the key of the constant folder's
+// deduplication, src/rewrite.rs:689-728): same type and form, same bytes.
+// Bytes on the host (or both still as literal text) compare directly;
+// otherwise the device hashes decide, and equal hashes are confirmed byte
+// for byte.
+bool value_eq(const DenseP& a, const DenseP& b, Engine& eng) {
   if (a == b) return true;
   if (a->poison || b->poison) return a->poison && b->poison && a->ty->text == b->ty->text;
   if (a->ty->text != b->ty->text || a->elements != b->elements || a->splat != b->splat || a->n != b->n) return false;
   if (!a->host.empty() && !b->host.empty()) return a->host == b->host;
-  if (!a->hex.empty() && !b->hex.empty()) return a->hex == b->hex;
-  return a->dev && a->dev == b->dev;
+  // Two literals still in their parsed text compare as text (mlir-opt
+  // prints hex bodies in one case), without uploading either.
+  if (!a->hex.empty() && !b->hex.empty() && !a->hashed && !b->hashed) return a->hex == b->hex;
+  if (!a->hex.empty() && !b->hex.empty() && a->hex == b->hex) return true;
+  if (a->dev && a->dev == b->dev) return true;
+  if (eng.device() < 0) {  // host-only: only bytes the host can read compare
+    auto readable = [](const DenseValue& v) { return !v.host.empty() || (!v.hex.empty() && v.hex.size() <= 8192); };
+    if (!readable(*a) || !readable(*b)) return false;
+    eng.to_host(*a);
+    eng.to_host(*b);
+    return a->host == b->host;
+  }
+  if (eng.hash_of(*a) != eng.hash_of(*b)) return false;
+  eng.to_host(*a);
+  eng.to_host(*b);
+  return a->host == b->host;
 }
 
 }  // namespace
@@ -1021,7 +1040,7 @@ struct Greedy::Impl {
     const std::string dialect = op->dialect();
     const std::string ty = op->results[0]->ty->text;
     for (auto& k : known)
-      if (k.region == r && k.dialect == dialect && k.ty == ty && value_eq(k.value, op->cst)) {
+      if (k.region == r && k.dialect == dialect && k.ty == ty && value_eq(k.value, op->cst, eng)) {
         replace_op(op, k.op->results);
         return false;
       }

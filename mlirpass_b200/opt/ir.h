@@ -108,6 +108,8 @@ struct DenseValue {
   std::string_view hex;      // "HEX…" digits (no 0x), when parsed from text
   std::shared_ptr<DeviceBuf> dev;  // device bytes
   int all_equal = -1;        // cached "every value equal" test: -1 unknown
+  uint64_t hash = 0;         // dcf_hash_many_async of the bytes, when hashed
+  bool hashed = false;
 
   bool on_host() const { return !host.empty() || n == 0; }
   uint64_t bits0() const;    // first element's bits (host bytes required)

@@ -47,6 +47,8 @@ def lib() -> ctypes.CDLL:
         L.dco_float_convert_bits.restype = u64
         L.dco_round_from_double.argtypes = [i, ctypes.c_double]
         L.dco_round_from_double.restype = u64
+        L.dco_hash.argtypes = [vp, u64]
+        L.dco_hash.restype = u64
         _lib = L
     return _lib
 
@@ -142,3 +144,8 @@ def float_convert_bits(from_dtype, to_dtype, bits):
     ok = ctypes.c_int(0)
     r = lib().dco_float_convert_bits(DTYPES[from_dtype], DTYPES[to_dtype], bits, ctypes.byref(ok))
     return bool(ok.value), int(r)
+
+
+def hash_bytes(data) -> int:
+    a = np.frombuffer(bytes(data), dtype=np.uint8)
+    return int(lib().dco_hash(_p(a) if len(a) else None, len(a)))

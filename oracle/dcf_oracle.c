@@ -811,3 +811,24 @@ int dco_splat_check(const void* in, size_t es, uint64_t n) {
     if (memcmp(b, b + i * es, es) != 0) return 0;
   return 1;
 }
+
+/* The 64-bit byte hash of dcf_hash_many_async (the documented formula):
+ * sum over 8-byte little-endian words w_i (the last zero-padded) of
+ * mix(w_i ^ i * 0x9E3779B97F4A7C15) plus mix(nbytes), mix being the
+ * SplitMix64 finaliser. */
+static uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+uint64_t dco_hash(const void* data, uint64_t nbytes) {
+  const uint8_t* b = (const uint8_t*)data;
+  uint64_t h = 0, nw = (nbytes + 7) / 8;
+  for (uint64_t i = 0; i < nw; i++) {
+    uint64_t w = 0;
+    for (uint64_t k = 0; k < 8 && 8 * i + k < nbytes; k++) w |= (uint64_t)b[8 * i + k] << (8 * k);
+    h += mix64(w ^ (i * 0x9E3779B97F4A7C15ull));
+  }
+  return h + mix64(nbytes);
+}

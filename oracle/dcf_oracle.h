@@ -43,6 +43,8 @@ int dco_hex_encode(const void* in, uint64_t nbytes, char* out);
 int dco_hex_decode(const char* in, uint64_t nchars, void* out);
 int dco_splat_check(const void* in, size_t elem_size, uint64_t n);
 
+uint64_t dco_hash(const void* data, uint64_t nbytes);
+
 /* Scalar helpers exposed for the golden-vector tests. */
 uint64_t dco_float_convert_bits(int from, int to, uint64_t bits, int* ok);
 uint64_t dco_round_from_double(int to, double x);

@@ -283,3 +283,31 @@ def test_pinned_text_gives_the_same_module():
     assert a == b and sa["folds"] == sb["folds"] == 3 * 40 + 1
     t2 = mlir_gen.config2_text(512)
     assert opt.run(t2, "canonicalize")[0] == opt.run(opt.pinned_text(t2), "canonicalize")[0]
+
+
+def test_equal_folded_constants_are_deduplicated(oracle):
+    # Two folds with bitwise-equal results (addf is commutative on these
+    # NaN-free operands) and a parsed constant with the same bytes become one
+    # constant, as the constant folder's Attribute-equality dedup makes them
+    # (src/rewrite.rs:689-728).
+    n = 1 << 16
+    c = W.config2(256)
+    a, b = c["A"][:n], c["B"][:n]
+    s = oracle.binary("addf", "f32", a, b).out
+    T = f"tensor<{n}xf32>"
+    h = lambda x: np.ascontiguousarray(x).view(np.uint32).tobytes().hex().upper()
+    body = "\n".join([
+        f'    %a = "arith.constant"() <{{value = dense<"0x{h(a)}"> : {T}}}> : () -> {T}',
+        f'    %b = "arith.constant"() <{{value = dense<"0x{h(b)}"> : {T}}}> : () -> {T}',
+        f'    %s = "arith.constant"() <{{value = dense<"0x{h(s)}"> : {T}}}> : () -> {T}',
+        f'    %0 = "arith.addf"(%a, %b) <{{fastmath = #arith.fastmath<none>}}> : ({T}, {T}) -> {T}',
+        f'    %1 = "arith.addf"(%b, %a) <{{fastmath = #arith.fastmath<none>}}> : ({T}, {T}) -> {T}'])
+    text = ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({T}, {T}, {T}), sym_name = "main"}}> ({{\n{body}\n'
+            f'    "func.return"(%0, %1, %s) : ({T}, {T}, {T}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
+    out, st = opt.run(text, "canonicalize")
+    f = parse_funcs(out)["main"]
+    assert len(set(f.ret.operands)) == 1, out[-300:]
+    assert [o.name for o in f.ops] == ["arith.constant", "func.return"]
+    d = f.defs[f.ret.operands[0]]
+    assert np.array_equal(np.array(d.const.bits, dtype=np.uint64), s.astype(np.uint64))

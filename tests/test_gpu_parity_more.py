@@ -176,3 +176,30 @@ def test_permute_groups_take_the_transpose(dcf, oracle):
     for perms in [(1, 2, 0), (2, 0, 1), (0, 2, 1)]:
         f = dcf.transpose(x, x.shape, perms)
         assert np.array_equal(f.out, oracle.transpose(x, x.shape, perms)), perms
+
+
+def test_hash_many(dcf, oracle):
+    import ctypes
+    import torch
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(8)
+    sizes = [0, 1, 7, 8, 9, 100, 4096, 65537, 1 << 20]
+    blob = rng.integers(0, 256, sum(sizes) + 64 * len(sizes), dtype=np.uint8)
+    d = torch.from_numpy(blob).to(dev)
+
+    class Piece(ctypes.Structure):
+        _fields_ = [("data", ctypes.c_void_p), ("nbytes", ctypes.c_uint64)]
+    arr = (Piece * len(sizes))()
+    offs, o = [], 0
+    for i, n in enumerate(sizes):
+        o += i % 5                  # unaligned starts too
+        offs.append(o)
+        arr[i].data, arr[i].nbytes = d.data_ptr() + o, n
+        o += n + 8
+    dp = torch.from_numpy(np.frombuffer(bytes(arr), dtype=np.uint8).copy()).to(dev)
+    out = torch.empty(len(sizes), dtype=torch.int64, device=dev)
+    assert dcf.lib().dcf_hash_many_async(dp.data_ptr(), len(sizes), max(sizes), out.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream) == 0
+    got = out.cpu().numpy().view(np.uint64)
+    for i, (o, n) in enumerate(zip(offs, sizes)):
+        assert int(got[i]) == oracle.hash_bytes(blob[o:o + n].tobytes()), (i, n)

@@ -422,3 +422,25 @@ def test_select(oracle):
     assert list(oracle.select(c, t, e).out) == [0, 11, 2, 13, 4]
     f = oracle.select(np.array([0], np.uint8), t, np.array([7], np.uint32), n=5, cond_splat=True, f_splat=True)
     assert list(f.out) == [7] * 5 and f.is_splat
+
+
+def test_byte_hash_formula(oracle):
+    # The documented dedup hash, restated in Python.
+    M = (1 << 64) - 1
+
+    def mix(z):
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        return z ^ (z >> 31)
+
+    def py_hash(b):
+        h = 0
+        for i in range(0, (len(b) + 7) // 8):
+            w = int.from_bytes(b[8 * i:8 * i + 8], "little")
+            h = (h + mix(w ^ ((i * 0x9E3779B97F4A7C15) & M))) & M
+        return (h + mix(len(b))) & M
+
+    rng = np.random.default_rng(4)
+    for n in (0, 1, 7, 8, 9, 64, 1000, 4097):
+        b = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+        assert oracle.hash_bytes(b) == py_hash(b), n
