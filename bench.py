@@ -560,16 +560,21 @@ def run_pass(args):
     # The module text is read from page-locked host memory (the driver then
     # copies constants straight from it), unless --pageable.
     src = text if args.pageable else opt.pinned_text(text)
+    for n_gpus in ([int(x) for x in args.sweep_gpus.split(",")] if args.sweep_gpus else [args.gpus]):
+        _pass_line(args, opt, cfg, pipe, text, src, n_gpus)
+
+
+def _pass_line(args, opt, cfg, pipe, text, src, n_gpus):
     runs = []
     for r in range(max(1, args.warmup) + args.steps):
         t0 = time.perf_counter()
-        out, st = opt.run(src, pipe, n_gpus=args.gpus, as_array=True)
+        out, st = opt.run(src, pipe, n_gpus=n_gpus, as_array=True)
         st["wall_ms"] = (time.perf_counter() - t0) * 1e3
         del out
         if r >= max(1, args.warmup):
             runs.append(st)
     best = min(runs, key=lambda s: s["run_ms"])
-    line = {"workload": f"pass {cfg}", "pipeline": pipe, "n_gpus": args.gpus, "text_bytes": len(text),
+    line = {"workload": f"pass {cfg}", "pipeline": pipe, "n_gpus": n_gpus, "text_bytes": len(text),
             "text_memory": "pageable" if args.pageable else "pinned",
             "parse_ms": round(best["parse_ms"], 2), "run_ms": round(best["run_ms"], 3),
             "run_ms_mean": round(statistics.mean(s["run_ms"] for s in runs), 3),
@@ -596,6 +601,7 @@ def main():
                          "pass:<config1|config2|config3-i8|...|config5>")
     ap.add_argument("--funcs", type=int, default=4096, help="functions of config 5")
     ap.add_argument("--pageable", action="store_true", help="pass workloads: keep the module text in pageable memory")
+    ap.add_argument("--sweep-gpus", default="", help="pass workloads: GPU counts to run in turn, e.g. 1,2,4,8")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -38,11 +38,21 @@ typedef struct dcf_opt_stats {
  * on GPUs 0..n_gpus-1 (n_gpus < 0: every GPU).  n_gpus == 0 runs host-only:
  * parsing, printing and the folds decided without element work (shortcuts)
  * succeed, and any fold that needs element work fails with an error; there
- * is no CPU fallback.  Chunks separated by "// -----" are run separately
- * when split_input_file is nonzero.  On success *out is a malloc'ed
+ * is no CPU fallback.  `flags` is a mask of DCF_OPT_* bits: with
+ * DCF_OPT_SPLIT_INPUT_FILE chunks separated by "// -----" lines are run
+ * separately; with DCF_OPT_LOCAL_SCOPE (mlir-opt's --mlir-print-local-scope)
+ * a module is not followed by a blank line; with DCF_OPT_DEBUGINFO
+ * (--mlir-print-debuginfo) locations are printed, without it op and block
+ * argument locations and `#loc` aliases are dropped.  Alias definitions
+ * that the printed module does not use are dropped.  On success *out is a
+ * malloc'ed
  * printed module (free with dcf_opt_free) and the return value is 0;
  * otherwise a negative code and dcf_opt_last_error() says why. */
-int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int split_input_file,
+#define DCF_OPT_SPLIT_INPUT_FILE 1
+#define DCF_OPT_LOCAL_SCOPE 2
+#define DCF_OPT_DEBUGINFO 4
+
+int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int flags,
                 char** out, size_t* out_len, dcf_opt_stats* stats);
 
 void dcf_opt_free(char* p);

@@ -412,6 +412,25 @@ void flatten_list(const std::string& s, std::vector<std::string>& out) {
   }
 }
 
+// Position of the first " loc(" in `t` outside brackets and string
+// literals (where a trailing location starts), or npos.
+size_t top_level_loc(const std::string& t) {
+  int depth = 0;
+  for (size_t k = 0; k < t.size(); k++) {
+    const char c = t[k];
+    if (c == '"') {
+      while (++k < t.size() && t[k] != '"')
+        if (t[k] == '\\') k++;
+      continue;
+    }
+    if (c == '-' && k + 1 < t.size() && t[k + 1] == '>') k++;  // an arrow, not a bracket
+    else if (c == '<' || c == '(' || c == '[' || c == '{') depth++;
+    else if (c == '>' || c == ')' || c == ']' || c == '}') depth--;
+    else if (depth == 0 && t.compare(k, 5, " loc(") == 0) return k;
+  }
+  return std::string::npos;
+}
+
 class Parser {
  public:
   Parser(std::string_view s, Module& m) : s_(s), m_(m) { find_hex_literals(); }
@@ -419,8 +438,49 @@ class Parser {
   Op* parse_top() {
     scopes_.emplace_back();
     ws();
+    // Alias definitions before the module op, one per line.
+    const size_t pro0 = p_;
+    while (p_ < s_.size() && (s_[p_] == '#' || s_[p_] == '!')) {
+      const size_t nl = s_.find('\n', p_);
+      p_ = nl == std::string_view::npos ? s_.size() : nl + 1;
+      ws();
+    }
+    m_.prologue = s_.substr(pro0, p_ - pro0);
+    if (p_ == s_.size()) {
+      // Nothing but blank lines and comments: an empty module, as a parser
+      // that wraps top-level ops in an implicit module makes of it.
+      Op* op = m_.new_op("builtin.module");
+      Region* r = m_.new_region();
+      r->parent = op;
+      Block* b = m_.new_block();
+      b->parent = r;
+      r->blocks.push_back(b);
+      op->regions.push_back(r);
+      close_scope();
+      return op;
+    }
     Op* op = parse_op(nullptr);
     ws();
+    // After it: location / attribute alias lines and metadata blocks.
+    const size_t epi0 = p_;
+    for (;;) {
+      if (p_ < s_.size() && (s_[p_] == '#' || s_[p_] == '!')) {
+        const size_t nl = s_.find('\n', p_);
+        p_ = nl == std::string_view::npos ? s_.size() : nl + 1;
+        m_.epilogue = s_.substr(epi0, p_ - epi0);
+        ws();
+        continue;
+      }
+      if (s_.compare(p_, 3, "{-#") == 0) {
+        const size_t a = p_ + 3, e = s_.find("#-}", a);
+        if (e == std::string_view::npos) fail("unterminated {-# block", p_);
+        m_.metadata.push_back(s_.substr(a, e - a));
+        p_ = e + 3;
+        ws();
+        continue;
+      }
+      break;
+    }
     if (p_ != s_.size()) fail("trailing text", p_);
     close_scope();
     return op;
@@ -647,7 +707,14 @@ class Parser {
           std::string name = ident();
           expect(':');
           std::string ty = span(",)");
+          // A trailing location belongs to the argument, not its type.
+          std::string loc;
+          if (const size_t k = top_level_loc(ty); k != std::string::npos) {
+            loc = ty.substr(k + 1);
+            ty.resize(k);
+          }
           Value* v = m_.new_value(type_of(ty));
+          v->loc = loc;
           v->owner = b;
           v->index = (int)b->args.size();
           v->name = name;
@@ -760,8 +827,8 @@ class Parser {
     }
     expect(':');
     std::string fnty = span("\n");
-    // trailing location
-    const size_t locp = fnty.rfind(" loc(");
+    // trailing location: the first " loc(" outside brackets and strings
+    const size_t locp = top_level_loc(fnty);
     if (locp != std::string::npos) {
       op->loc = fnty.substr(locp + 1);
       fnty = trim(fnty.substr(0, locp));
@@ -770,9 +837,13 @@ class Parser {
       int depth = 0;
       for (size_t i = 0; i + 1 < fnty.size(); i++) {
         const char c = fnty[i];
+        if (c == '-' && fnty[i + 1] == '>') {  // an arrow, nested (a function type) or the top one
+          if (depth == 0) return i;
+          i++;
+          continue;
+        }
         if (c == '(' || c == '<' || c == '[' || c == '{') depth++;
         if (c == ')' || c == '>' || c == ']' || c == '}') depth--;
-        if (c == '-' && fnty[i + 1] == '>' && depth == 0) return i;
       }
       return std::string::npos;
     }();
@@ -943,14 +1014,41 @@ class Printer {
   Printer(const PrintHooks& h) : h_(h) {}
   std::string out;
 
+  // SSA names as the reference's generic printer spells them (Names::of,
+  // src/ir.rs:2636-2650 with Namer, :2470-2635): one value counter and one
+  // entry-block-argument counter for the whole module, never reset; regions
+  // are named from a stack, so after a region's own blocks come the regions
+  // nested in it, the last one first.  Entry-block arguments are %argK,
+  // other block arguments and op results %N, an op with several results
+  // %N:k with uses %N#i.
+  void assign_names(Op* root) {
+    uint64_t vnext = 0, anext = 0;
+    std::vector<Region*> stack(root->regions.begin(), root->regions.end());
+    while (!stack.empty()) {
+      Region* r = stack.back();
+      stack.pop_back();
+      for (size_t bi = 0; bi < r->blocks.size(); bi++) {
+        Block* b = r->blocks[bi];
+        for (Value* a : b->args)
+          names_[a] = bi == 0 ? "%arg" + std::to_string(anext++) : "%" + std::to_string(vnext++);
+        for (Op* o : b->ops) {
+          if (o->results.empty()) continue;
+          const std::string name = "%" + std::to_string(vnext++);
+          defs_[o] = name;
+          for (size_t i = 0; i < o->results.size(); i++)
+            names_[o->results[i]] = o->results.size() == 1 ? name : name + "#" + std::to_string(i);
+        }
+      }
+      for (Block* b : r->blocks)
+        for (Op* o : b->ops)
+          for (Region* nr : o->regions) stack.push_back(nr);
+    }
+  }
+
   void op(Op* o, int indent) {
     out.append(indent, ' ');
     if (!o->results.empty()) {
-      const int base = next_++;
-      const std::string name = "%" + std::to_string(base);
-      for (size_t i = 0; i < o->results.size(); i++)
-        names_[o->results[i]] = o->results.size() == 1 ? name : name + "#" + std::to_string(i);
-      out += name;
+      out += defs_[o];
       if (o->results.size() > 1) out += ":" + std::to_string(o->results.size());
       out += " = ";
     }
@@ -960,7 +1058,7 @@ class Printer {
       out += name_of(o->operands[i]);
     }
     out += ")";
-    if (!o->successors.empty()) out += o->successors;
+    if (!o->successors.empty()) out += successors(o);
     if (!o->props.empty() || (o->cst && !o->cst_text && !o->cst->poison)) {
       out += " <{";
       bool first = true;
@@ -970,7 +1068,7 @@ class Printer {
         if (!first) out += ", ";
         first = false;
         out += kv.first;
-        if (o->cst && !o->cst_text && kv.first == key) {
+        if (o->cst && !o->cst_text && !o->cst->poison && kv.first == key) {
           out += " = ";
           put_value(*o->cst);
           wrote_value = true;
@@ -988,15 +1086,11 @@ class Printer {
       }
       out += "}>";
     }
-    const bool isolated = o->name == "func.func" || o->name == "builtin.module";
     if (!o->regions.empty()) {
       out += " (";
       for (size_t r = 0; r < o->regions.size(); r++) {
         if (r) out += ", ";
-        int saved_next = next_, saved_arg = arg_;
-        if (isolated) next_ = 0, arg_ = 0;
         region(o->regions[r], indent);
-        if (isolated) next_ = saved_next, arg_ = saved_arg;
       }
       out += ")";
     }
@@ -1017,7 +1111,7 @@ class Printer {
       }
       out += ")";
     }
-    if (!o->loc.empty()) out += " " + o->loc;
+    if (!o->loc.empty() && h_.debuginfo) out += " " + o->loc;
     out += "\n";
   }
 
@@ -1032,8 +1126,33 @@ class Printer {
   const PrintHooks& h_;
   std::unordered_map<Value*, std::string> names_;
 
+  std::unordered_map<Op*, std::string> defs_;
+
   void defer(Fill::Kind k, const void* src, size_t nchars) { fills.push_back({k, src, nchars, out.size()}); }
-  int next_ = 0, arg_ = 0;
+
+  // The successor list with every block label spelled ^bbN, N the block's
+  // position in the region (as the reference prints labels).
+  std::string successors(Op* o) {
+    const std::string& t = o->successors;
+    Region* r = o->parent ? o->parent->parent : nullptr;
+    if (!r) return t;
+    std::string res;
+    for (size_t i = 0; i < t.size();) {
+      if (t[i] != '^') {
+        res += t[i++];
+        continue;
+      }
+      size_t j = i + 1;
+      while (j < t.size() && (isalnum((unsigned char)t[j]) || strchr("_$.-", t[j]))) j++;
+      const std::string label = t.substr(i, j - i);
+      size_t idx = r->blocks.size();
+      for (size_t k = 0; k < r->blocks.size(); k++)
+        if (r->blocks[k]->label == label) idx = k;
+      res += idx < r->blocks.size() ? "^bb" + std::to_string(idx) : label;
+      i = j;
+    }
+    return res;
+  }
 
   std::string name_of(Value* v) {
     auto it = names_.find(v);
@@ -1041,23 +1160,64 @@ class Printer {
     return "%<undefined>";
   }
 
+  // Each block's predecessors, one entry per branch edge, by block index.
+  static std::vector<std::vector<size_t>> predecessors(Region* r) {
+    std::vector<std::vector<size_t>> preds(r->blocks.size());
+    if (r->blocks.size() < 2) return preds;
+    std::unordered_map<std::string_view, size_t> index;
+    for (size_t k = 0; k < r->blocks.size(); k++) index.emplace(r->blocks[k]->label, k);
+    for (size_t k = 0; k < r->blocks.size(); k++)
+      for (Op* o : r->blocks[k]->ops)
+        for_each_label(o->successors, [&](std::string_view l) {
+          auto it = index.find(l);
+          if (it != index.end()) preds[it->second].push_back(k);
+        });
+    return preds;
+  }
+
+  template <class F>
+  static void for_each_label(const std::string& t, F&& f) {
+    for (size_t i = 0; i < t.size(); i++) {
+      if (t[i] != '^') continue;
+      size_t j = i + 1;
+      while (j < t.size() && (isalnum((unsigned char)t[j]) || strchr("_$.-", t[j]))) j++;
+      f(std::string_view(t).substr(i, j - i));
+      i = j - 1;
+    }
+  }
+
+  // Blocks as mlir-opt writes them in the generic form: the entry block's
+  // header only when it has arguments or no ops, every other block with a
+  // comment naming its predecessors (sorted by position, one per edge).
   void region(Region* r, int indent) {
     out += "{\n";
+    const auto preds = predecessors(r);
     for (size_t bi = 0; bi < r->blocks.size(); bi++) {
       Block* b = r->blocks[bi];
-      for (Value* a : b->args) names_[a] = "%arg" + std::to_string(arg_++);
-      if (!b->args.empty() || bi > 0) {
+      if (!b->args.empty() || bi > 0 || b->ops.empty()) {
         out.append(indent, ' ');
-        out += b->label.empty() ? "^bb" + std::to_string(bi) : b->label;
+        out += "^bb" + std::to_string(bi);
         if (!b->args.empty()) {
           out += "(";
           for (size_t i = 0; i < b->args.size(); i++) {
             if (i) out += ", ";
             out += names_[b->args[i]] + ": " + b->args[i]->ty->text;
+            if (!b->args[i]->loc.empty() && h_.debuginfo) out += " " + b->args[i]->loc;
           }
           out += ")";
         }
-        out += ":\n";
+        out += ":";
+        if (bi > 0) {
+          std::vector<size_t> p = preds[bi];
+          std::sort(p.begin(), p.end());
+          if (p.empty()) {
+            out += "  // no predecessors";
+          } else {
+            out += p.size() == 1 ? "  // pred: " : "  // " + std::to_string(p.size()) + " preds: ";
+            for (size_t k = 0; k < p.size(); k++) out += (k ? ", ^bb" : "^bb") + std::to_string(p[k]);
+          }
+        }
+        out += "\n";
       }
       for (Op* o : b->ops) op(o, indent + 2);
     }
@@ -1133,10 +1293,158 @@ static size_t estimate(const Op* o) {
   return n;
 }
 
+// Names of the dense_resource blobs the module still refers to.
+static void used_resources(const Op* o, std::vector<std::string>& out) {
+  auto scan = [&](std::string_view t) {
+    for (size_t at = t.find("dense_resource<"); at != std::string_view::npos; at = t.find("dense_resource<", at + 1)) {
+      const size_t a = at + 15, b = t.find('>', a);
+      if (b != std::string_view::npos) out.emplace_back(t.substr(a, b - a));
+    }
+  };
+  for (auto& kv : o->props) scan(kv.second);
+  scan(o->big_value);
+  scan(o->attrs);
+  for (const Region* r : o->regions)
+    for (const Block* b : r->blocks)
+      for (const Op* in : b->ops) used_resources(in, out);
+}
+
+// A metadata block as the reference prints it back
+// (src/ir.rs:2951-2974): in a dialect_resources block only the blobs still
+// used stay (the last kept one loses its trailing comma), and a block left
+// with none is dropped.
+static bool keep_resources(std::string_view body, const std::vector<std::string>& used, std::string& out) {
+  if (body.find("dialect_resources") == std::string_view::npos) {
+    out.assign(body);
+    return true;
+  }
+  std::vector<std::string_view> lines;
+  for (size_t a = 0;;) {
+    const size_t b = body.find('\n', a);
+    lines.push_back(body.substr(a, b == std::string_view::npos ? std::string_view::npos : b - a));
+    if (b == std::string_view::npos) break;
+    a = b + 1;
+  }
+  auto blob = [](std::string_view l) -> std::string_view {
+    const size_t c = l.find(": \"0x");
+    if (c == std::string_view::npos) return {};
+    std::string_view k = l.substr(0, c);
+    while (!k.empty() && isspace((unsigned char)k.front())) k.remove_prefix(1);
+    while (!k.empty() && isspace((unsigned char)k.back())) k.remove_suffix(1);
+    return k;
+  };
+  std::vector<std::string_view> kept;
+  size_t n = 0;
+  for (std::string_view l : lines) {
+    const std::string_view k = blob(l);
+    if (k.empty()) {
+      kept.push_back(l);
+      continue;
+    }
+    if (std::find(used.begin(), used.end(), std::string(k)) == used.end()) continue;
+    kept.push_back(l);
+    n++;
+  }
+  if (n == 0) return false;
+  out.clear();
+  size_t seen = 0;
+  for (size_t i = 0; i < kept.size(); i++) {
+    std::string_view l = kept[i];
+    if (!blob(l).empty() && ++seen == n)
+      while (!l.empty() && l.back() == ',') l.remove_suffix(1);
+    if (i) out += '\n';
+    out.append(l);
+  }
+  return true;
+}
+
+// Alias definition lines (`#name = ...`, `!name = ...`) that are printed,
+// after Invocation::print_op (src/pass.rs:769-793): location aliases only
+// with debuginfo, and of the others those the printed module uses (`#name`
+// not followed by another name character), directly or through another
+// printed alias.  `head` and `tail` receive the kept lines of the text
+// before and after the module op.
+struct AliasLine {
+  std::string_view line, name;
+  bool tail, loc, kept = false;
+};
+
+static bool names(std::string_view text, std::string_view name) {
+  auto name_char = [](char c) { return isalnum((unsigned char)c) || strchr("_$.-", c); };
+  for (size_t at = text.find(name); at != std::string_view::npos; at = text.find(name, at + 1))
+    if (at + name.size() >= text.size() || !name_char(text[at + name.size()])) return true;
+  return false;
+}
+
+static void kept_aliases(std::string_view pro, std::string_view epi, std::string_view rest, bool debuginfo,
+                         std::string& head, std::string& tail) {
+  auto name_char = [](char c) { return isalnum((unsigned char)c) || strchr("_$.-", c); };
+  std::vector<AliasLine> al;
+  for (int part = 0; part < 2; part++) {
+    const std::string_view lines = part ? epi : pro;
+    for (size_t a = 0; a < lines.size();) {
+      size_t e = lines.find('\n', a);
+      e = e == std::string_view::npos ? lines.size() : e + 1;
+      const std::string_view line = lines.substr(a, e - a);
+      a = e;
+      if (line.empty() || (line[0] != '#' && line[0] != '!')) continue;
+      size_t n = 1;
+      while (n < line.size() && name_char(line[n])) n++;
+      const size_t eq = line.find('=', n);
+      if (eq == std::string_view::npos) continue;
+      size_t v = eq + 1;
+      while (v < line.size() && line[v] == ' ') v++;
+      al.push_back({line, line.substr(0, n), part == 1, line[0] == '#' && line.compare(v, 4, "loc(") == 0});
+    }
+  }
+  for (auto& x : al) x.kept = (debuginfo || !x.loc) && names(rest, x.name);
+  for (bool grew = true; grew;) {
+    grew = false;
+    for (auto& x : al) {
+      if (x.kept || (x.loc && !debuginfo)) continue;
+      for (const auto& y : al)
+        if (y.kept && names(y.line.substr(y.name.size()), x.name)) {
+          x.kept = grew = true;
+          break;
+        }
+    }
+  }
+  for (const auto& x : al) {
+    if (!x.kept) continue;
+    std::string& out = x.tail ? tail : head;
+    out.append(x.line);
+    if (out.back() != '\n') out += '\n';
+  }
+}
+
 PrintedModule print_module_parts(Module& m, const PrintHooks& hooks) {
   Printer p(hooks);
-  p.out.reserve(estimate(m.top));
+  p.out.reserve(estimate(m.top) + m.prologue.size() + m.epilogue.size());
+  p.assign_names(m.top);
   p.op(m.top, 0);
+  std::string meta;
+  if (!m.metadata.empty()) {
+    std::vector<std::string> used;
+    used_resources(m.top, used);
+    for (std::string_view body : m.metadata) {
+      std::string kept;
+      if (!keep_resources(body, used, kept)) continue;
+      meta += "\n{-#";
+      meta += kept;
+      meta += "#-}\n";
+    }
+  }
+  if (!m.prologue.empty() || !m.epilogue.empty()) {
+    const std::string rest = p.out + meta;
+    std::string head, tail;
+    kept_aliases(m.prologue, m.epilogue, rest, hooks.debuginfo, head, tail);
+    p.out += tail;
+    if (!head.empty()) {
+      p.out.insert(0, head);
+      for (auto& f : p.fills) f.at += head.size();
+    }
+  }
+  p.out += meta;
   PrintedModule r;
   r.skeleton = std::move(p.out);
   r.fills = std::move(p.fills);

@@ -130,6 +130,7 @@ struct Value {
   Block* owner = nullptr;     // block of a block argument
   std::vector<Op*> uses;      // one entry per operand slot that reads it
   std::string name;           // text name of a block argument ("%arg0")
+  std::string loc;            // a block argument's trailing "loc(...)"
 };
 
 struct Op {
@@ -172,6 +173,13 @@ struct Region {
 class Module {
  public:
   Op* top = nullptr;          // the builtin.module op
+  // Text around the module op, kept verbatim: alias definitions before and
+  // after it (`#map = ...`, `!t = ...`, `#loc = loc(...)` lines) and
+  // `{-# ... #-}` metadata blocks (dialect resources) after it (the bodies
+  // between the markers).
+  std::string_view prologue;
+  std::string_view epilogue;  // alias lines after the module op
+  std::vector<std::string_view> metadata;
 
   Op* new_op(const std::string& name);
   Value* new_value(TypeP ty);
@@ -209,6 +217,9 @@ struct PrintHooks {
   // Host bytes of a splat's element (fetch from the device if needed).
   uint64_t (*bits0_of)(DenseValue& v, void* ctx) = nullptr;
   void* ctx = nullptr;
+  // Print locations (mlir-opt's --mlir-print-debuginfo); without it op and
+  // block-argument locations and `#loc` alias lines are left out.
+  bool debuginfo = false;
 };
 // A printed module: the text without its large literal bodies, plus where
 // each body goes.  write_to() assembles the text with several host threads

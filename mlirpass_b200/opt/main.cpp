@@ -1,5 +1,6 @@
 // main.cpp — the C ABI (include/dcfold_opt.h) and the `dcfold-opt` command
 // line of the pass driver.
+#include <cctype>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -66,20 +67,29 @@ bool is_pinned(std::string_view text) {
   return true;
 }
 
+// Chunks of --split-input-file: the text between lines that read exactly
+// "// -----" (trailing blanks allowed), as Invocation::chunks splits
+// (src/pass.rs:704-716).
 std::vector<std::string_view> split_chunks(std::string_view text, bool split) {
   std::vector<std::string_view> out;
   if (!split) {
     out.push_back(text);
     return out;
   }
-  size_t a = 0;
-  for (;;) {
-    const size_t b = text.find("// -----", a);
-    out.push_back(text.substr(a, b == std::string_view::npos ? std::string_view::npos : b - a));
-    if (b == std::string_view::npos) break;
-    const size_t nl = text.find('\n', b);
-    a = nl == std::string_view::npos ? text.size() : nl + 1;
+  static constexpr std::string_view kMarker = "// -----";
+  size_t start = 0;
+  for (size_t at = 0; at < text.size();) {
+    size_t nl = text.find('\n', at);
+    const size_t end = nl == std::string_view::npos ? text.size() : nl + 1;
+    std::string_view line = text.substr(at, end - at);
+    while (!line.empty() && isspace((unsigned char)line.back())) line.remove_suffix(1);
+    if (line == kMarker) {
+      out.push_back(text.substr(start, at - start));
+      start = end;
+    }
+    at = end;
   }
+  out.push_back(text.substr(start));
   return out;
 }
 
@@ -89,10 +99,11 @@ struct Output {
   size_t n = 0;
 };
 
-Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, bool split, dcf_opt_stats* st) {
+Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, int flags, dcf_opt_stats* st) {
   Engines eng(n_gpus);
   dcf_opt_stats total{};
-  const auto chunks = split_chunks(text, split);
+  const auto chunks = split_chunks(text, (flags & DCF_OPT_SPLIT_INPUT_FILE) != 0);
+  const size_t tail = (flags & DCF_OPT_LOCAL_SCOPE) ? 0 : 1;
   // Modules stay alive until the text is assembled: the printed parts
   // point into their constants.
   std::vector<std::unique_ptr<dco::Module>> mods;
@@ -116,13 +127,17 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, b
     hooks.hex_of = hex_hook;
     hooks.bits0_of = bits_hook;
     hooks.ctx = &eng;
+    hooks.debuginfo = (flags & DCF_OPT_DEBUGINFO) != 0;
     parts.push_back(dco::print_module_parts(m, hooks));
     total.print_ms += ms_since(t0);
   }
   auto t0 = Clock::now();
+  // Each chunk's module and, unless printing in local scope, one more
+  // newline; the chunks joined by the marker line (Invocation::print and
+  // Invocation::run, src/pass.rs:761-767 and :817-820).
   static const char sep[] = "// -----\n";
   Output out;
-  for (size_t i = 0; i < parts.size(); i++) out.n += parts[i].size() + (i ? sizeof sep - 1 : 0);
+  for (size_t i = 0; i < parts.size(); i++) out.n += parts[i].size() + tail + (i ? sizeof sep - 1 : 0);
   out.p = (char*)malloc(out.n + 1);
   if (!out.p) throw std::runtime_error("out of memory for the printed module");
   size_t at = 0;
@@ -133,6 +148,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, b
     }
     parts[i].write_to(out.p + at);
     at += parts[i].size();
+    if (tail) out.p[at++] = '\n';
   }
   out.p[out.n] = 0;
   total.print_ms += ms_since(t0);
@@ -150,14 +166,14 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, b
 
 }  // namespace
 
-extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int split_input_file,
+extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int flags,
                            char** out, size_t* out_len, dcf_opt_stats* stats) {
   if (!text || !pipeline || !out) {
     g_opt_err = "null argument";
     return -1;
   }
   try {
-    const Output r = run_all(std::string_view(text, len), pipeline, n_gpus, split_input_file != 0, stats);
+    const Output r = run_all(std::string_view(text, len), pipeline, n_gpus, flags, stats);
     *out = r.p;
     if (out_len) *out_len = r.n;
     return 0;
@@ -175,7 +191,8 @@ extern "C" const char* dcf_opt_last_error(void) { return g_opt_err.c_str(); }
 int main(int argc, char** argv) {
   std::string input = "-", output = "-", pipeline;
   int gpus = 1;
-  bool split = false, timing = false;
+  int flags = 0;
+  bool timing = false;
   for (int i = 1; i < argc; i++) {
     std::string a = argv[i];
     if (a == "--canonicalize" || a == "-canonicalize" || a.rfind("--canonicalize=", 0) == 0 ||
@@ -184,7 +201,11 @@ int main(int argc, char** argv) {
     else if (a.rfind("--pass-pipeline=", 0) == 0 || a.rfind("-pass-pipeline=", 0) == 0)
       pipeline = a.substr(a.find('=') + 1);
     else if (a == "--split-input-file" || a == "-split-input-file")
-      split = true;
+      flags |= DCF_OPT_SPLIT_INPUT_FILE;
+    else if (a == "--mlir-print-local-scope" || a == "-mlir-print-local-scope")
+      flags |= DCF_OPT_LOCAL_SCOPE;
+    else if (a == "--mlir-print-debuginfo" || a == "-mlir-print-debuginfo")
+      flags |= DCF_OPT_DEBUGINFO;
     else if (a.rfind("--gpus=", 0) == 0)
       gpus = atoi(a.c_str() + 7);
     else if (a == "--timing")
@@ -218,7 +239,7 @@ int main(int argc, char** argv) {
   const std::string text = buf.str();
   dcf_opt_stats st{};
   try {
-    const Output r = run_all(text, pipeline, gpus, split, &st);
+    const Output r = run_all(text, pipeline, gpus, flags, &st);
     if (output == "-") fwrite(r.p, 1, r.n, stdout);
     else {
       std::ofstream f(output, std::ios::binary);
