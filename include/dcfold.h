@@ -134,7 +134,42 @@ typedef enum dcf_op {
   DCF_TRUNCI = 74,
   /* tosa.reciprocal, 1/x round-to-nearest-even
    * (src/patterns/tosa/canonicalize.rs:596-605; layerwise pass) */
-  DCF_RECIPROCAL = 80
+  DCF_RECIPROCAL = 80,
+  /* math dialect folds that are exact (ArithFolder::math,
+   * src/patterns/math/canonicalize.rs:145-234), unary through dcf_convert
+   * with from == to:
+   *   absf        sign cleared (every float type)
+   *   ceil, floor, roundeven
+   *               to an integral value; a NaN comes back quieted (every
+   *               float type, FloatFolds::integral :87-92)
+   *   round, trunc, sqrt
+   *               f32 / f64 only (any other type refuses); sqrt refuses a
+   *               negative operand (sign bit set, -0 and -NaN included);
+   *               a NaN comes back quieted
+   *   rsqrt       1 / sqrt(x) rounded twice, f32 / f64 only; refuses a
+   *               negative operand; a NaN comes back quieted
+   *   absi (wrapping), ctlz, cttz, ctpop (of zero: the width)
+   * and binary through dcf_binary:
+   *   copysign    lhs with rhs's sign bit (every float type)
+   *   ipowi       wrapping power by squaring; a negative exponent gives
+   *               1 for base 1, +-1 for base -1 by parity, 0 otherwise,
+   *               and refuses base 0; i1 refuses (IntFolds::ipowi :95-124)
+   * The inexact ones (sin, exp, log, pow, ...) are the host C library's
+   * results in the reference and are not offered. */
+  DCF_ABSF = 96,
+  DCF_CEIL = 97,
+  DCF_FLOOR = 98,
+  DCF_ROUNDEVEN = 99,
+  DCF_ROUND = 100,
+  DCF_TRUNC = 101,
+  DCF_SQRT = 102,
+  DCF_RSQRT = 103,
+  DCF_ABSI = 104,
+  DCF_CTLZ = 105,
+  DCF_CTTZ = 106,
+  DCF_CTPOP = 107,
+  DCF_COPYSIGN = 112,
+  DCF_IPOWI = 113
 } dcf_op;
 
 /* Flags word.
@@ -241,9 +276,10 @@ int dcf_binary(dcf_op op, dcf_dtype dtype, const void* lhs, int lhs_splat,
                void* out, dcf_result* res);
 
 /* Elementwise conversion fold (extf, truncf, sitofp, uitofp, fptosi,
- * fptoui, negf, flush_denormals, extsi, extui, trunci) from `from` to
- * `to`.  Replaces the Const::map closures at
- * src/patterns/arith/canonicalize.rs:327-333, 376-434, 685-762. */
+ * fptoui, negf, flush_denormals, extsi, extui, trunci, and the unary math
+ * folds with from == to) from `from` to `to`.  Replaces the Const::map
+ * closures at src/patterns/arith/canonicalize.rs:327-333, 376-434, 685-762
+ * and src/patterns/math/canonicalize.rs:127-234. */
 int dcf_convert(dcf_op op, dcf_dtype from, dcf_dtype to, const void* in,
                 int in_splat, uint64_t n, uint32_t flags, void* out,
                 dcf_result* res);

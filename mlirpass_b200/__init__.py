@@ -43,13 +43,18 @@ OPS = {
     "extf": 64, "truncf": 65, "sitofp": 66, "uitofp": 67, "fptosi": 68, "fptoui": 69,
     "negf": 70, "flush_denormals": 71, "extsi": 72, "extui": 73, "trunci": 74,
     "reciprocal": 80,
+    # math dialect (exact folds only)
+    "absf": 96, "ceil": 97, "floor": 98, "roundeven": 99, "round": 100, "trunc": 101, "sqrt": 102,
+    "rsqrt": 103, "absi": 104, "ctlz": 105, "cttz": 106, "ctpop": 107, "copysign": 112, "ipowi": 113,
 }
-BINARY_OPS = tuple(k for k, v in OPS.items() if v < 64)
-FLOAT_BINARY_OPS = tuple(k for k, v in OPS.items() if v < 16 or k == "cmpf")
+BINARY_OPS = tuple(k for k, v in OPS.items() if v < 64 or k in ("copysign", "ipowi"))
+FLOAT_BINARY_OPS = tuple(k for k, v in OPS.items() if v < 16 or k in ("cmpf", "copysign"))
+MATH_FLOAT_UNARY_OPS = ("absf", "ceil", "floor", "roundeven", "round", "trunc", "sqrt", "rsqrt")
+MATH_INT_UNARY_OPS = ("absi", "ctlz", "cttz", "ctpop")
 INT_BINARY_OPS = tuple(k for k in BINARY_OPS if k not in FLOAT_BINARY_OPS)
 BOOL_RESULT_OPS = ("cmpi", "cmpf", "addui_carry")
 CONVERT_OPS = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "negf", "flush_denormals", "extsi",
-               "extui", "trunci")
+               "extui", "trunci") + MATH_FLOAT_UNARY_OPS + MATH_INT_UNARY_OPS
 
 FLAG_PRED_SHIFT = 8
 FLAG_NEG_DEFAULT_NAN = 1 << 16

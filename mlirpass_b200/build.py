@@ -27,7 +27,7 @@ ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libdcforacle.so")
 # (template-heavy) translation units compile in parallel.
 SOURCES = ["dcf_ew_float.cu", "dcf_ew_float_f32.cu", "dcf_ew_float_f64.cu", "dcf_ew_float_h.cu",
            "dcf_ew_float_f8.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_ew_convert_ff.cu",
-           "dcf_ew_convert_if.cu", "dcf_ew_convert_fi.cu", "dcf_misc.cu", "dcf_transpose_tma.cu", "dcf_runtime.cu",
+           "dcf_ew_convert_if.cu", "dcf_ew_convert_fi.cu", "dcf_ew_math.cu", "dcf_misc.cu", "dcf_transpose_tma.cu", "dcf_runtime.cu",
            "dcf_noalloc.cu"]
 
 NVCC_FLAGS = [

@@ -36,7 +36,7 @@ int launch_convert(const EwLaunch& a) {
       });
     }
     default:
-      return DCF_EUNSUPPORTED;
+      return launch_math_unary(a);
   }
 }
 

@@ -68,6 +68,44 @@ template <int W> struct ICarry {
   }
 };
 
+// math.ipowi (IntFolds::ipowi, src/patterns/math/canonicalize.rs:95-124):
+// the exponent is signed; a negative one gives 1 for base 1, +-1 for base
+// -1 by its parity and 0 for any other base except 0, which refuses; a
+// non-negative one is a wrapping power by squaring.  An i1 base refuses
+// (:163).
+template <int W> struct IPow {
+  using I = IntW<W>;
+  using In = typename I::T;
+  using Out = typename I::T;
+  static constexpr bool kBinary = true;
+  __device__ static __forceinline__ bool apply(In a, In b, uint32_t, Out& o) {
+    o = 0;
+    if constexpr (W == 1) {
+      return false;
+    } else {
+      const uint64_t base = (uint64_t)a & I::MASK, pw = (uint64_t)b & I::MASK;
+      if (pw == 0) {
+        o = 1;
+        return true;
+      }
+      if (I::sx(pw) < 0) {
+        if (base == 0) return false;
+        o = (Out)(base == 1 ? 1 : base != I::MASK ? 0 : (pw & 1) ? I::MASK : 1);
+        return true;
+      }
+      uint64_t r = 1, x = base, p = pw;
+      for (;;) {
+        if (p & 1) r = (r * x) & I::MASK;
+        p >>= 1;
+        if (!p) break;
+        x = (x * x) & I::MASK;
+      }
+      o = (Out)r;
+      return true;
+    }
+  }
+};
+
 template <int W> static int int_binary_for(const EwLaunch& a) {
   switch (a.op) {
     case DCF_ADDI: return launch_one<IOp<DCF_ADDI, W>>(a);
@@ -94,6 +132,7 @@ template <int W> static int int_binary_for(const EwLaunch& a) {
     case DCF_MULUI_HI: return launch_one<IOp<DCF_MULUI_HI, W>>(a);
     case DCF_CMPI: return launch_one<ICmp<W>>(a);
     case DCF_ADDUI_CARRY: return launch_one<ICarry<W>>(a);
+    case DCF_IPOWI: return launch_one<IPow<W>>(a);
     default: return DCF_EUNSUPPORTED;
   }
 }

@@ -1,5 +1,5 @@
 // dcf_float_ops.cuh — functors of the float folds (addf, subf, mulf, divf,
-// remf, the four min/max ops, dense cmpf, tosa reciprocal) and their
+// remf, the four min/max ops, dense cmpf, copysign, tosa reciprocal) and their
 // per-layout dispatch.  Each float layout is instantiated in its own
 // translation unit (dcf_ew_float_*.cu) so the library builds in parallel.
 #pragma once
@@ -69,6 +69,18 @@ template <class L> struct FRecip {
   }
 };
 
+// math.copysign (src/patterns/math/canonicalize.rs:153-156): lhs negated
+// when the signs differ, i.e. lhs with rhs's sign bit.
+template <class L> struct FCopySign {
+  using In = typename L::T;
+  using Out = typename L::T;
+  static constexpr bool kBinary = true;
+  __device__ static __forceinline__ bool apply(In a, In b, uint32_t, Out& o) {
+    o = (Out)(((uint64_t)a & ~L::SIGN) | ((uint64_t)b & L::SIGN));
+    return true;
+  }
+};
+
 template <int OP, class L> int arith_for(const EwLaunch& a) {
   if ((a.flags & DCF_FLAG_ROUND_MASK) == 0) return launch_one<FArith<OP, L, true>>(a);
   return launch_one<FArith<OP, L, false>>(a);
@@ -86,6 +98,7 @@ template <class L> int float_binary_for(const EwLaunch& a) {
     case DCF_MINNUMF: return launch_one<FMinMax<L, false, false>>(a);
     case DCF_REMF: return launch_one<FRem<L>>(a);
     case DCF_CMPF: return launch_one<FCmp<L>>(a);
+    case DCF_COPYSIGN: return launch_one<FCopySign<L>>(a);
     default: return DCF_EUNSUPPORTED;
   }
 }

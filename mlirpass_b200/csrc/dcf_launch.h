@@ -44,14 +44,21 @@ struct EwLaunch {
 
 // Op classes (one place for the runtime, the batch entry points and the
 // kernel dispatch).
-inline bool op_float_binary(int op) { return (op >= DCF_ADDF && op <= DCF_REMF) || op == DCF_CMPF; }
-inline bool op_int_binary(int op) {
-  return (op >= DCF_ADDI && op <= DCF_MULUI_HI) || op == DCF_CMPI || op == DCF_ADDUI_CARRY;
+inline bool op_float_binary(int op) {
+  return (op >= DCF_ADDF && op <= DCF_REMF) || op == DCF_CMPF || op == DCF_COPYSIGN;
 }
+inline bool op_int_binary(int op) {
+  return (op >= DCF_ADDI && op <= DCF_MULUI_HI) || op == DCF_CMPI || op == DCF_ADDUI_CARRY || op == DCF_IPOWI;
+}
+// Unary math folds (element type unchanged), float and integer.
+inline bool op_math_float_unary(int op) { return op >= DCF_ABSF && op <= DCF_RSQRT; }
+inline bool op_math_int_unary(int op) { return op >= DCF_ABSI && op <= DCF_CTPOP; }
 inline bool op_binary(int op) { return op_float_binary(op) || op_int_binary(op); }
 // Binary ops whose result elements are i1 bytes.
 inline bool op_bool_result(int op) { return op == DCF_CMPI || op == DCF_CMPF || op == DCF_ADDUI_CARRY; }
-inline bool op_convert(int op) { return op >= DCF_EXTF && op <= DCF_TRUNCI; }
+inline bool op_convert(int op) {
+  return (op >= DCF_EXTF && op <= DCF_TRUNCI) || op_math_float_unary(op) || op_math_int_unary(op);
+}
 // Whether a conversion op accepts the (from, to) element types.
 inline bool convert_types_ok(int op, bool from_float, bool from_int, bool to_float, bool to_int, int from, int to) {
   switch (op) {
@@ -60,7 +67,10 @@ inline bool convert_types_ok(int op, bool from_float, bool from_int, bool to_flo
     case DCF_FPTOSI: case DCF_FPTOUI: return from_float && to_int;
     case DCF_NEGF: case DCF_FLUSH_DENORMALS: return from_float && from == to;
     case DCF_EXTSI: case DCF_EXTUI: case DCF_TRUNCI: return from_int && to_int;
-    default: return false;
+    default:
+      if (op_math_float_unary(op)) return from_float && from == to;
+      if (op_math_int_unary(op)) return from_int && from == to;
+      return false;
   }
 }
 
@@ -70,6 +80,7 @@ int launch_float_binary(const EwLaunch& a);    // addf..minnumf, cmpf
 int launch_int_binary(const EwLaunch& a);      // addi..minui, cmpi
 int launch_convert(const EwLaunch& a);         // extf, truncf, si/uitofp, fptosi/ui
 int launch_reciprocal(const EwLaunch& a);
+int launch_math_unary(const EwLaunch& a);     // absf..rsqrt, absi..ctpop
 
 // With a status, 2-byte transposes take the bulk-tensor kernel when the
 // shapes and alignment allow (its bounded waits report through st->error).

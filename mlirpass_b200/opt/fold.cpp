@@ -209,6 +209,33 @@ class ArithFolder {
     for (Value* v : op->operands) c_.push_back(constant_of(v));
   }
 
+  // ArithFolder::math, src/patterns/math/canonicalize.rs:145-234.  The
+  // exact element folds run on the GPU; the classification ops decide on
+  // the host from a splat operand (:136-143); the inexact ones (sin, exp,
+  // log, pow, ...; the host C library's results in the reference) are not
+  // folded.
+  Plan math() {
+    const std::string& name = op_->name;
+    if (name.rfind("math.", 0) != 0 || op_->results.size() != 1) return Plan::failed();
+    const std::string o = name.substr(5);
+    static const std::pair<const char*, int> float_ops[] = {
+        {"absf", DCF_ABSF},   {"ceil", DCF_CEIL},   {"floor", DCF_FLOOR}, {"roundeven", DCF_ROUNDEVEN},
+        {"round", DCF_ROUND}, {"trunc", DCF_TRUNC}, {"sqrt", DCF_SQRT},   {"rsqrt", DCF_RSQRT}};
+    static const std::pair<const char*, int> int_ops[] = {
+        {"absi", DCF_ABSI}, {"ctlz", DCF_CTLZ}, {"cttz", DCF_CTTZ}, {"ctpop", DCF_CTPOP}};
+    for (const auto& [n, code] : float_ops)
+      if (o == n) return float_unary(code);
+    for (const auto& [n, code] : int_ops)
+      if (o == n) {
+        if (!element_type(ty())->is_int()) return Plan::failed();
+        return unary(code, element_type(ty())->dtype);
+      }
+    if (o == "copysign") return binary(DCF_COPYSIGN, 0, nullptr);
+    if (o == "ipowi") return binary(DCF_IPOWI, 0, nullptr);
+    if (o == "isfinite" || o == "isinf" || o == "isnan" || o == "isnormal") return classify(o);
+    return Plan::failed();
+  }
+
   // ArithFolder::fold, src/patterns/arith/canonicalize.rs:270-491.
   Plan fold() {
     const std::string& name = op_->name;
@@ -638,6 +665,25 @@ class ArithFolder {
 
   // bitcast (:764-789): the same bits under the result's element type, so
   // no element work; the new constant shares the operand's bytes.
+  // Folder::classify (math/canonicalize.rs:136-143): a splat float operand
+  // gives an i1 splat (a scalar for a scalar operand).
+  Plan classify(const std::string& o) {
+    DenseP k = cst(0);
+    FloatBits f;
+    if (!k || !k->splat || !k->ty->is_float() || !float_layout(k->dtype, &f)) return Plan::failed();
+    const uint64_t b = eng_.bits0_of(*k), emax = (1ull << f.E) - 1;
+    const uint64_t e = (b >> f.M) & emax, m = b & ((1ull << f.M) - 1);
+    const bool nan = e == emax && m != 0, inf = e == emax && m == 0;
+    bool v;
+    if (o == "isfinite") v = !nan && !inf;
+    else if (o == "isinf") v = inf;
+    else if (o == "isnan") v = nan;
+    else v = e != 0 && e != emax;  // FloatFolds::is_normal (:94-98)
+    TypeP rty = ty();
+    if (!element_type(rty)->is_int() || (rty->shaped() && rty->dynamic)) return Plan::failed();
+    return Plan::of_attr(splat_value(rty, v ? 1 : 0));
+  }
+
   Plan bitcast() {
     if (!c_.size() || !c_[0]) return Plan::failed();
     DenseP a = c_[0];
@@ -1096,6 +1142,7 @@ struct Greedy::Impl {
     Plan own;
     const std::string d = op->dialect();
     if (d == "arith") own = ArithFolder(m, op, eng).fold();
+    else if (d == "math") own = ArithFolder(m, op, eng).math();
     else if (d == "tosa") own = tosa_fold(m, op, eng);
     if (own.k == Plan::FAILED) return fold_traits(op);
     const bool to_self = own.k == Plan::VALUE && op->results.size() == 1 && own.value == op->results[0];

@@ -527,6 +527,27 @@ static void res_finish(dcf_result* res, const void* out, int ob, uint64_t n) {
   res->is_splat = (uint8_t)dco_splat_check(out, (size_t)ob, n);
 }
 
+/* IntFolds::ipowi (src/patterns/math/canonicalize.rs:95-124), with the i1
+ * refusal of the math.ipowi closure (:163). */
+static int ipowi(int w, uint64_t a, uint64_t b, uint64_t* out) {
+  uint64_t m = wmask(w), base = a & m, p = b & m, result = 1;
+  if (w == 1) return 0;
+  if (p == 0) { *out = 1; return 1; }
+  if (sext(p, w) < 0) {
+    if (base == 0) return 0;
+    if (base == 1) *out = 1;
+    else if (base != m) *out = 0;
+    else *out = (p & 1) ? m : 1;
+    return 1;
+  }
+  for (;;) {
+    if (p & 1) result = (result * base) & m;
+    p >>= 1;
+    if (p == 0) { *out = result; return 1; }
+    base = (base * base) & m;
+  }
+}
+
 /* Folder::binary loop, src/patterns/arith/canonicalize.rs:214-216:
  * (0..n).map(|i| f(l.at(i), r.at(i))).collect::<Option<Vec<_>>>() */
 int dco_binary(int op, int dtype, const void* lhs, int lhs_splat,
@@ -542,7 +563,7 @@ int dco_binary(int op, int dtype, const void* lhs, int lhs_splat,
   int isf = fl_of(dtype, &f);
   int pred = (int)((flags & DCF_FLAG_PRED_MASK) >> DCF_FLAG_PRED_SHIFT);
   int mode = (int)(flags & DCF_FLAG_ROUND_MASK);
-  int fop = op >= DCF_ADDF && op <= DCF_REMF;
+  int fop = (op >= DCF_ADDF && op <= DCF_REMF) || op == DCF_COPYSIGN;
   if ((fop || op == DCF_CMPF) && !isf) return DCF_EINVAL;
   if (!fop && op != DCF_CMPF && !w) return DCF_EINVAL;
   for (uint64_t i = 0; i < n; i++) {
@@ -561,6 +582,13 @@ int dco_binary(int op, int dtype, const void* lhs, int lhs_splat,
       case DCF_CMPF: r = (uint64_t)cmpf(pred, f, a, b); break;
       case DCF_CMPI: r = (uint64_t)cmpi(pred, w, a, b); break;
       case DCF_REMF: r = remf(f, a, b, flags); break;
+      /* math.copysign (src/patterns/math/canonicalize.rs:153-156) */
+      case DCF_COPYSIGN: {
+        uint64_t sign = 1ull << (f.E + f.M);
+        r = (f_sign(f, a) != f_sign(f, b)) ? a ^ sign : a;
+        break;
+      }
+      case DCF_IPOWI: ok = ipowi(w, a, b, &r); break;
       case DCF_ADDUI_CARRY:                                    /* :887-891 */
         r = (uint64_t)((((a & wmask(w)) + (b & wmask(w))) & wmask(w)) < (a & wmask(w)));
         break;
@@ -663,6 +691,63 @@ static int float_to_int(fl_t from, uint64_t b, int w, int is_signed, uint64_t* o
   return 1;
 }
 
+/* The exact unary math folds, ArithFolder::math
+ * (src/patterns/math/canonicalize.rs:145-234). */
+static int math_unary(int op, int dtype, fl_t f, int w, uint64_t a, uint64_t* out) {
+  uint64_t sign = 1ull << (f.E + f.M);
+  switch (op) {
+    case DCF_ABSF: *out = f_sign(f, a) ? a ^ sign : a; return 1;   /* :150 */
+    case DCF_CEIL: case DCF_FLOOR: case DCF_ROUNDEVEN: {            /* :151-153 */
+      /* FloatFolds::integral (:87-92): NaN quieted, else libm
+       * ceil / floor / rint of to_f64, back with from_f64 */
+      double x, y;
+      if (f_isnan(f, a)) { *out = f_quiet(f, a); return 1; }
+      x = f_to_double(f, a);
+      y = op == DCF_CEIL ? ceil(x) : op == DCF_FLOOR ? floor(x) : nearbyint(x);
+      *out = f_convert(F64L, f, double_bits(y));
+      return 1;
+    }
+    case DCF_ROUND: case DCF_TRUNC: case DCF_SQRT: case DCF_RSQRT: {
+      /* the exact cmath functions (:47-51, :219-233) and rsqrt (:166-171):
+       * f32 / f64 only; sqrt and rsqrt refuse a negative operand; a NaN of
+       * the exact functions comes back quieted, and 1 / sqrt(NaN) is the
+       * same quieted NaN */
+      if (dtype != DCF_F32 && dtype != DCF_F64) return 0;
+      if ((op == DCF_SQRT || op == DCF_RSQRT) && f_sign(f, a)) return 0;
+      if (f_isnan(f, a)) { *out = f_quiet(f, a); return 1; }
+      if (dtype == DCF_F32) {
+        float x = bits_float((uint32_t)a), y;
+        if (op == DCF_ROUND) y = roundf(x);
+        else if (op == DCF_TRUNC) y = truncf(x);
+        else if (op == DCF_SQRT) y = sqrtf(x);
+        else y = 1.0f / sqrtf(x);
+        *out = float_bits(y);
+      } else {
+        double x = bits_double(a), y;
+        if (op == DCF_ROUND) y = round(x);
+        else if (op == DCF_TRUNC) y = trunc(x);
+        else if (op == DCF_SQRT) y = sqrt(x);
+        else y = 1.0 / sqrt(x);
+        *out = double_bits(y);
+      }
+      return 1;
+    }
+    /* ApInt neg / count_leading_zeros / count_trailing_zeros / popcount
+     * (:157-160); the count of a zero is the width */
+    case DCF_ABSI: *out = sext(a, w) < 0 ? (0 - a) & wmask(w) : a & wmask(w); return 1;
+    case DCF_CTLZ: case DCF_CTTZ: case DCF_CTPOP: {
+      uint64_t v = a & wmask(w), n = 0;
+      int k;
+      if (op == DCF_CTPOP) { for (k = 0; k < w; k++) n += (v >> k) & 1; }
+      else if (op == DCF_CTLZ) { for (k = w - 1; k >= 0 && !((v >> k) & 1); k--) n++; }
+      else { for (k = 0; k < w && !((v >> k) & 1); k++) n++; }
+      *out = n;
+      return 1;
+    }
+    default: return 0;
+  }
+}
+
 /* Folder::unary -> Const::map with the conversion closures. */
 int dco_convert(int op, int from, int to, const void* in, int in_splat,
                 uint64_t n, uint32_t flags, void* out, dcf_result* res) {
@@ -679,6 +764,13 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
     case DCF_FPTOSI: case DCF_FPTOUI: if (!fromf || !wt) return DCF_EINVAL; break;
     case DCF_NEGF: case DCF_FLUSH_DENORMALS: if (!fromf || from != to) return DCF_EINVAL; break;
     case DCF_EXTSI: case DCF_EXTUI: case DCF_TRUNCI: if (!wf || !wt) return DCF_EINVAL; break;
+    case DCF_ABSF: case DCF_CEIL: case DCF_FLOOR: case DCF_ROUNDEVEN:
+    case DCF_ROUND: case DCF_TRUNC: case DCF_SQRT: case DCF_RSQRT:
+      if (!fromf || from != to) return DCF_EINVAL;
+      break;
+    case DCF_ABSI: case DCF_CTLZ: case DCF_CTTZ: case DCF_CTPOP:
+      if (!wf || from != to) return DCF_EINVAL;
+      break;
     default: return DCF_EINVAL;
   }
   for (uint64_t i = 0; i < n; i++) {
@@ -698,7 +790,8 @@ int dco_convert(int op, int from, int to, const void* in, int in_splat,
         break;
       /* ApInt sext / zext / trunc (:388-398, :685-706) */
       case DCF_EXTSI: r = (uint64_t)sext(a, wf) & wmask(wt); break;
-      default: r = a & wmask(wf) & wmask(wt); break;
+      case DCF_EXTUI: case DCF_TRUNCI: r = a & wmask(wf) & wmask(wt); break;
+      default: ok = math_unary(op, from, ff, wf, a, &r); break;
     }
     if (!ok) {
       if (res) res->first_fail_index = i;

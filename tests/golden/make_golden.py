@@ -8,12 +8,14 @@ It reads mlirpass's `tests/fixtures/<stem>.in.mlir` (the input, as
 mlir-opt 23.1.5 prints it) and `<stem>.generic.mlir` (mlir-opt's output of
 the fixture's canonicalize RUN line), for every fixture whose pipeline is a
 plain canonicalize.  For each function, every value returned by `func.return`
-that is produced by a hot-path fold op whose operands are all constants
-becomes one case; the expected outcome is read at the same return position
-of the output function: a constant (folded, with its value) or the same op
+or stored by `memref.store` that is produced by a hot-path fold op whose
+operands are all constants becomes one case; the expected outcome is read at
+the same position of the output function: a constant (folded, with its value) or the same op
 (not folded).  Cases the output rewrote into something else are dropped.
 
-Each case is also labelled with the shortcut, if any, that ArithFolder::fold
+Math dialect fixtures (ArithFolder::math, src/patterns/math/canonicalize.rs)
+contribute the exact folds.  Each case is also labelled with the shortcut,
+if any, that ArithFolder::fold
 (src/patterns/arith/canonicalize.rs:270-491) or Tf::fold
 (src/patterns/tosa/canonicalize.rs:189-232) takes before the per-element
 loop, so element-level tests can select the cases that reach the loop.
@@ -44,6 +46,10 @@ CMP = {"cmpi", "cmpf"}
 EXTENDED = {"addui_extended", "subui_extended", "mulsi_extended", "mului_extended"}
 ARITH = BINARY_F | BINARY_I | CONVERT | CMP | {"select"} | EXTENDED
 TOSA = {"reciprocal", "transpose"}
+# math dialect folds with an exact result (the transcendental ones are the
+# host C library's values in the reference and have no device restatement)
+MATH = {"absf", "ceil", "floor", "roundeven", "round", "trunc", "sqrt", "rsqrt", "absi", "ctlz", "cttz", "ctpop",
+        "copysign", "ipowi", "isfinite", "isinf", "isnan", "isnormal"}
 
 ALLOWED_FLAGS = ("-split-input-file", "--split-input-file", "-allow-unregistered-dialect",
                  "--allow-unregistered-dialect")
@@ -193,6 +199,13 @@ def shortcut(op: str, ops, consts, props) -> str | None:
     return None
 
 
+def sinks(f):
+    """The values a function observes, in order: those it stores with
+    memref.store, then those it returns."""
+    out = [op.operands[0] for op in f.ops if op.name == "memref.store" and op.operands]
+    return out + list(f.ret.operands)
+
+
 def main():
     cases = []
     stems = sorted(f[:-5] for f in os.listdir(FIX) if f.endswith(".args"))
@@ -215,14 +228,16 @@ def main():
                 g = fout.get(name)
                 if g is None or f.ret is None or g.ret is None:
                     continue
-                if len(f.ret.operands) != len(g.ret.operands):
+                fs, gs = sinks(f), sinks(g)
+                if len(fs) != len(gs):
                     continue
-                for pos, v in enumerate(f.ret.operands):
+                for pos, (v, gv) in enumerate(zip(fs, gs)):
                     op = f.defs.get(v)
                     if op is None or "." not in op.name:
                         continue
                     dialect, short = op.name.split(".", 1)
-                    if not ((dialect == "arith" and short in ARITH) or (dialect == "tosa" and short in TOSA)):
+                    if not ((dialect == "arith" and short in ARITH) or (dialect == "tosa" and short in TOSA)
+                            or (dialect == "math" and short in MATH)):
                         continue
                     opnds = [f.defs.get(o) for o in op.operands]
                     if short == "transpose":
@@ -238,7 +253,6 @@ def main():
                     res_ty = parse_type(op.out_types[k])
                     if res_ty is None:
                         continue
-                    gv = g.ret.operands[pos]
                     gop = g.defs.get(gv)
                     if gop is None:
                         continue

@@ -24,7 +24,12 @@ SIZE = {"i1": 1, "i8": 1, "i16": 2, "i32": 4, "i64": 8, "index": 8, "f16": 2, "b
 CANON = {"index": "i64"}
 EXTENDED = ("addui_extended", "subui_extended", "mulsi_extended", "mului_extended")
 UNARY = ("extf", "truncf", "sitofp", "uitofp", "fptosi", "fptoui", "convertf", "negf", "flush_denormals", "extsi",
-         "extui", "trunci", "index_cast", "index_castui")
+         "extui", "trunci", "index_cast", "index_castui",
+         # math (same type in and out)
+         "absf", "ceil", "floor", "roundeven", "round", "trunc", "sqrt", "rsqrt", "absi", "ctlz", "cttz", "ctpop")
+CLASSIFY = ("isfinite", "isinf", "isnan", "isnormal")
+FLOAT_BITS = {"f16": (5, 10), "bf16": (8, 7), "f32": (8, 23), "f64": (11, 52), "f8E5M2": (5, 2), "f8E4M3": (4, 3),
+              "f8E3M4": (3, 4)}
 
 
 def load_cases():
@@ -69,6 +74,17 @@ def run_case(c, eng):
         else:
             raise ValueError(op)
         return ("folded", (True, [int(x) for x in f.out[:1]])) if f.folded else ("not_folded", None)
+    if dialect == "math" and op in CLASSIFY:
+        # Folder::classify (src/patterns/math/canonicalize.rs:136-143): a
+        # splat float operand only, decided on the host.
+        if not ops[0]["splat"]:
+            return "not_folded", None
+        E, M = FLOAT_BITS[ops[0]["dtype"]]
+        b = int(ops[0]["bits"][0], 16)
+        e, m, emax = (b >> M) & ((1 << E) - 1), b & ((1 << M) - 1), (1 << E) - 1
+        nan, inf = e == emax and m != 0, e == emax and m == 0
+        v = {"isfinite": not nan and not inf, "isinf": inf, "isnan": nan, "isnormal": e not in (0, emax)}[op]
+        return "folded", (True, [int(v)])
     if op == "bitcast":
         # ApInt::from_bits / ApFloat::from_bits of the same bits
         # (src/patterns/arith/canonicalize.rs:764-789): no element work.

@@ -311,3 +311,46 @@ def test_equal_folded_constants_are_deduplicated(oracle):
     assert [o.name for o in f.ops] == ["arith.constant", "func.return"]
     d = f.defs[f.ret.operands[0]]
     assert np.array_equal(np.array(d.const.bits, dtype=np.uint64), s.astype(np.uint64))
+
+
+def test_math_folds_through_canonicalize(oracle):
+    # The exact math folds at a size where every one is a device fold,
+    # through the whole driver, against the oracle; a transcendental op
+    # stays in place.
+    from test_gpu_parity import rbits
+    n = 1 << 18
+    F, I = f"tensor<{n}xf32>", f"tensor<{n}xi32>"
+    fa = rbits("f32", n, 11) & np.uint32(0x7FFFFFFF)   # non-negative: sqrt / rsqrt fold
+    fb = rbits("f32", n, 12)
+    x, y = rbits("i32", n, 13), (np.arange(n) % 37).astype(np.uint32)
+    fm = "<{fastmath = #arith.fastmath<none>}>"
+    ops = [("absf", "fb"), ("ceil", "fb"), ("floor", "fb"), ("roundeven", "fb"), ("round", "fb"),
+           ("trunc", "fb"), ("sqrt", "fa"), ("rsqrt", "fa")]
+    lines = [
+        f'    %fa = "arith.constant"() <{{value = dense<"0x{_hex(fa)}"> : {F}}}> : () -> {F}',
+        f'    %fb = "arith.constant"() <{{value = dense<"0x{_hex(fb)}"> : {F}}}> : () -> {F}',
+        f'    %x = "arith.constant"() <{{value = dense<"0x{_hex(x)}"> : {I}}}> : () -> {I}',
+        f'    %y = "arith.constant"() <{{value = dense<"0x{_hex(y)}"> : {I}}}> : () -> {I}',
+    ]
+    for i, (op, v) in enumerate(ops):
+        lines.append(f'    %{i} = "math.{op}"(%{v}) {fm} : ({F}) -> {F}')
+    k = len(ops)
+    lines += [f'    %{k} = "math.copysign"(%fa, %fb) {fm} : ({F}, {F}) -> {F}',
+              f'    %{k + 1} = "math.ctlz"(%x) : ({I}) -> {I}',
+              f'    %{k + 2} = "math.absi"(%x) : ({I}) -> {I}',
+              f'    %{k + 3} = "math.ipowi"(%x, %y) : ({I}, {I}) -> {I}',
+              f'    %{k + 4} = "math.exp"(%fa) {fm} : ({F}) -> {F}']
+    tys = [F] * (k + 1) + [I] * 3 + [F]
+    rets = [f"%{i}" for i in range(k + 5)]
+    text = ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({", ".join(tys)}), sym_name = "main"}}> ({{\n'
+            + "\n".join(lines) + f'\n    "func.return"({", ".join(rets)}) : ({", ".join(tys)}) -> ()\n'
+            '  }) : () -> ()\n}) : () -> ()\n')
+    out, st = opt.run(text, "canonicalize")
+    got = consts_returned(out)
+    assert [d.name for d in got] == ["arith.constant"] * (k + 4) + ["math.exp"]
+    want = [oracle.convert(op, "f32", "f32", fa if v == "fa" else fb).out for op, v in ops]
+    want += [oracle.binary("copysign", "f32", fa, fb).out, oracle.convert("ctlz", "i32", "i32", x).out,
+             oracle.convert("absi", "i32", "i32", x).out, oracle.binary("ipowi", "i32", x, y).out]
+    for i, (d, w) in enumerate(zip(got, want)):
+        assert np.array_equal(full(d, n), w.astype(np.uint64)), i

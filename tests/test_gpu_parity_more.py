@@ -203,3 +203,47 @@ def test_hash_many(dcf, oracle):
     got = out.cpu().numpy().view(np.uint64)
     for i, (o, n) in enumerate(zip(offs, sizes)):
         assert int(got[i]) == oracle.hash_bytes(blob[o:o + n].tobytes()), (i, n)
+
+
+MATH_F = ["absf", "ceil", "floor", "roundeven", "round", "trunc", "sqrt", "rsqrt"]
+
+
+@pytest.mark.parametrize("dt", FLOATS)
+@pytest.mark.parametrize("op", MATH_F)
+def test_math_float_unary_vs_oracle(op, dt, dcf, oracle):
+    # Random bits refuse sqrt / rsqrt at the first negative element; the
+    # same values with the sign cleared fold, so both outcomes are compared.
+    sign = {1: 0x80, 2: 0x8000, 4: 0x80000000, 8: 0x8000000000000000}[SZ[dt]]
+    for n in SIZES:
+        for mode in ("mixed", "raw"):
+            a = rbits(dt, n, 71 + n, mode)
+            same(dcf.convert(op, dt, dt, a), oracle.convert(op, dt, dt, a), n)
+            pos = a & a.dtype.type(~sign & ((1 << 8 * SZ[dt]) - 1))
+            same(dcf.convert(op, dt, dt, pos), oracle.convert(op, dt, dt, pos), n)
+    a = rbits(dt, 1, 9)
+    same(dcf.convert(op, dt, dt, a, n=4097, splat=True), oracle.convert(op, dt, dt, a, n=4097, splat=True), 4097)
+
+
+@pytest.mark.parametrize("dt", INTS)
+@pytest.mark.parametrize("op", ["absi", "ctlz", "cttz", "ctpop"])
+def test_math_int_unary_vs_oracle(op, dt, dcf, oracle):
+    for n in SIZES:
+        a = rbits(dt, n, 81 + n)
+        same(dcf.convert(op, dt, dt, a), oracle.convert(op, dt, dt, a), n)
+
+
+@pytest.mark.parametrize("dt", FLOATS)
+def test_copysign_vs_oracle(dt, dcf, oracle):
+    for n in SIZES:
+        a, b = rbits(dt, n, 91 + n, "raw"), rbits(dt, n, 92 + n, "raw")
+        same(dcf.binary("copysign", dt, a, b), oracle.binary("copysign", dt, a, b), n)
+
+
+@pytest.mark.parametrize("dt", INTS)
+def test_ipowi_vs_oracle(dt, dcf, oracle):
+    for n in SIZES:
+        a, b = rbits(dt, n, 93 + n), rbits(dt, n, 94 + n)
+        # small exponents and bases too, where the powers do not wrap to 0
+        small = (np.arange(n) % 7).astype(a.dtype)
+        for x, y in [(a, b), (small, b), (a, small), (np.where(a == 0, a.dtype.type(3), a), b)]:
+            same(dcf.binary("ipowi", dt, x, y), oracle.binary("ipowi", dt, x, y), n)

@@ -217,3 +217,28 @@ def test_output_as_array_without_copy():
     gc.collect()
     assert bytes(view) == opt.run(text, "canonicalize", n_gpus=0, as_bytes=True)[0][5:]
     assert st["call_ms"] > 0
+
+
+def test_math_classify_folds_on_the_host_and_transcendentals_stay():
+    F, V = "f32", "vector<4xf32>"
+    body = "\n".join([
+        const("%a", "2.000000e+00", F),
+        const("%b", "dense<0x7FC00000>", V),
+        '    %p = "ub.poison"() <{value = #ub.poison}> : () -> f32',
+        '    %0 = "math.isnormal"(%a) <{fastmath = #arith.fastmath<none>}> : (f32) -> i1',
+        '    %1 = "math.isnan"(%b) <{fastmath = #arith.fastmath<none>}> : (vector<4xf32>) -> vector<4xi1>',
+        '    %2 = "math.absf"(%p) <{fastmath = #arith.fastmath<none>}> : (f32) -> f32',
+        '    %3 = "math.sin"(%a) <{fastmath = #arith.fastmath<none>}> : (f32) -> f32',
+        '    %4 = "math.isinf"(%b) <{fastmath = #arith.fastmath<none>}> : (vector<4xf32>) -> vector<4xi1>',
+    ])
+    out = run(module(body, "%0, %1, %2, %3, %4", "i1, vector<4xi1>, f32, f32, vector<4xi1>"))
+    f = parse_funcs(out)["f"]
+    d = [f.defs[v] for v in f.ret.operands]
+    assert [x.name for x in d] == ["arith.constant", "arith.constant", "ub.poison", "math.sin", "arith.constant"]
+    assert d[0].const.bits == [1] and d[1].const.splat and d[1].const.bits == [1] and d[4].const.bits == [0]
+
+
+def test_math_element_folds_need_a_gpu():
+    body = const("%a", C4, T) + '\n    %0 = "math.ceil"(%a) <{fastmath = #arith.fastmath<none>}> : (tensor<4xf32>) -> tensor<4xf32>'
+    with pytest.raises(opt.OptError, match="needs a GPU"):
+        run(module(body, "%0", T))

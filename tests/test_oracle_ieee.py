@@ -444,3 +444,94 @@ def test_byte_hash_formula(oracle):
     for n in (0, 1, 7, 8, 9, 64, 1000, 4097):
         b = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
         assert oracle.hash_bytes(b) == py_hash(b), n
+
+
+@pytest.mark.parametrize("dt,np_t,ut", [("f32", np.float32, np.uint32), ("f64", np.float64, np.uint64)])
+def test_math_float_ops_match_numpy(dt, np_t, ut, oracle):
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.standard_normal(4000) * 10.0 ** rng.integers(-3, 8, 4000),
+                        np.array([0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 0.0, -0.0, np.inf, -np.inf, 4.0, 1e-300])
+                        ]).astype(np_t)
+    bits = x.view(ut)
+    def fold(op, v):
+        f = oracle.convert(op, dt, dt, v.view(ut))
+        assert f.folded, op
+        return f.out.view(np_t)
+    with np.errstate(all="ignore"):
+        for op, ref in [("absf", np.abs), ("ceil", np.ceil), ("floor", np.floor), ("roundeven", np.rint),
+                        ("trunc", np.trunc)]:
+            assert np.array_equal(fold(op, x).view(ut), ref(x).view(ut)), op
+        # round: half away from zero
+        r = np.where(x >= 0, np.floor(x + np_t(0.5)), -np.floor(-x + np_t(0.5)))
+        exact = np.abs(x) < 2.0 ** (23 if dt == "f32" else 52)
+        assert np.array_equal(fold("round", x)[exact], r[exact])
+        assert np.array_equal(fold("round", x)[~exact].view(ut), x[~exact].view(ut))
+        pos = np.abs(x)
+        pos = pos[pos.view(ut) != 0]     # +0 folds; -0 refuses (sign bit set)
+        assert np.array_equal(fold("sqrt", pos).view(ut), np.sqrt(pos).view(ut))
+        assert np.array_equal(fold("rsqrt", pos).view(ut), (np_t(1) / np.sqrt(pos)).view(ut))
+    # refusals: a set sign bit (-0 and -NaN too) for sqrt / rsqrt
+    for op in ("sqrt", "rsqrt"):
+        for v in (-0.0, -1.0, -np.nan):
+            f = oracle.convert(op, dt, dt, np.array([4.0, v], dtype=np_t).view(ut))
+            assert not f.folded and f.first_fail_index == 1
+    # NaN comes back quieted
+    snan = np.array([0x7F800001 if dt == "f32" else 0x7FF0000000000001], dtype=ut)
+    for op in ("ceil", "floor", "roundeven", "round", "trunc", "sqrt", "rsqrt"):
+        q = oracle.convert(op, dt, dt, snan).out
+        assert int(q[0]) == int(snan[0]) | (1 << (22 if dt == "f32" else 51)), op
+    # round / trunc / sqrt / rsqrt exist for f32 and f64 only
+    for op in ("round", "trunc", "sqrt", "rsqrt"):
+        assert not oracle.convert(op, "f16", "f16", np.array([0x3C00], np.uint16)).folded
+
+
+def test_math_integral_ops_on_narrow_floats(oracle):
+    # f16: every bit pattern against numpy's float16 rounding of the double
+    a = np.arange(1 << 16, dtype=np.uint16)
+    x = a.view(np.float16)
+    ok = ~np.isnan(x)
+    for op, ref in [("ceil", np.ceil), ("floor", np.floor), ("roundeven", np.rint)]:
+        got = oracle.convert(op, "f16", "f16", a).out
+        with np.errstate(invalid="ignore"):
+            want = ref(x.astype(np.float64)).astype(np.float16).view(np.uint16)
+        assert np.array_equal(got[ok], want[ok]), op
+        assert np.array_equal(got[~ok], a[~ok] | np.uint16(0x200)), op
+
+
+@pytest.mark.parametrize("w", [1, 8, 16, 32, 64])
+def test_math_int_ops_match_python(w, oracle):
+    dt = {1: "i1", 8: "i8", 16: "i16", 32: "i32", 64: "i64"}[w]
+    st = {1: np.uint8, 8: np.uint8, 16: np.uint16, 32: np.uint32, 64: np.uint64}[w]
+    rng = np.random.default_rng(w)
+    m = (1 << w) - 1
+    vals = [0, 1, m, m >> 1, (m >> 1) + 1] + [int(v) & m for v in rng.integers(0, 1 << 62, 200)]
+    a = np.array(vals, dtype=st)
+    def sx(v):
+        return v - (1 << w) if v >> (w - 1) else v
+    want = {
+        "absi": [abs(sx(v)) & m for v in vals],
+        "ctlz": [w - v.bit_length() for v in vals],
+        "cttz": [w if v == 0 else (v & -v).bit_length() - 1 for v in vals],
+        "ctpop": [bin(v).count("1") for v in vals],
+    }
+    for op, exp in want.items():
+        assert [int(x) for x in oracle.convert(op, dt, dt, a).out] == exp, op
+    b = np.array([int(v) % 9 for v in vals], dtype=st) if w > 1 else a
+    f = oracle.binary("ipowi", dt, a, b)
+    if w == 1:
+        assert not f.folded
+        return
+    assert [int(x) for x in f.out] == [pow(x, int(y), 1 << w) for x, y in zip(vals, b)]
+    # negative exponents: 1 for base 1, +-1 for base -1 by parity, else 0; base 0 refuses
+    neg = np.array([m, m - 1], dtype=st)
+    assert [int(x) for x in oracle.binary("ipowi", dt, np.array([1, m], st), neg).out] == [1, 1]
+    assert [int(x) for x in oracle.binary("ipowi", dt, np.array([m, 5], st), neg).out] == [m, 0]
+    assert not oracle.binary("ipowi", dt, np.array([0], st), np.array([m], st)).folded
+
+
+def test_copysign_matches_numpy(oracle):
+    rng = np.random.default_rng(5)
+    a = rng.integers(0, 1 << 32, 1000, dtype=np.uint64).astype(np.uint32)
+    b = rng.integers(0, 1 << 32, 1000, dtype=np.uint64).astype(np.uint32)
+    got = oracle.binary("copysign", "f32", a, b).out
+    assert np.array_equal(got, (a & np.uint32(0x7FFFFFFF)) | (b & np.uint32(0x80000000)))

@@ -44,6 +44,8 @@ def _jobs(seed):
         {"op": "cmpi", "dtype": "i64", "lhs": p, "rhs": q, "flags": 2 << 8,
          "out": torch.empty(n, dtype=torch.uint8, device=dev)},
         {"op": "addf", "dtype": "f32", "lhs": a[1:], "rhs": b[1:], "out": torch.empty(n - 1, device=dev)},
+        {"op": "rsqrt", "dtype": "f32", "out_dtype": "f32", "lhs": a.abs(), "out": torch.empty_like(a)},
+        {"op": "ipowi", "dtype": "i32", "lhs": x, "rhs": y, "out": torch.empty_like(x)},
     ]
 
 
