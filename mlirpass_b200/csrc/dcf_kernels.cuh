@@ -224,11 +224,7 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
 // in the status's error word, drains its copies (again bounded) and exits.
 constexpr int kTileBytes = 16384;
 constexpr int kStages = 2;
-// Resident CTAs per SM: three when two operands stream (192 KiB of tiles in
-// flight per SM), six when one does, so that a unary fold keeps as many
-// bytes in flight as a binary one.  DCF_TMA_CTAS_PER_SM overrides both.
 constexpr int kTmaCtasPerSm = 3;
-constexpr int kTmaCtasPerSmUnary = 6;
 constexpr long kWaitLimit = 1l << 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -448,7 +444,6 @@ __global__ void __launch_bounds__(kThreads) ew_batch_kernel(const BatchDesc* __r
 int grid_for(uint64_t work_items, const void* kernel);
 int sm_count_current();
 int tma_min_tiles_per_sm();
-int tma_ctas_per_sm(int streamed);
 bool prepare_smem(const void* kernel, int bytes);
 
 template <class F>
@@ -477,8 +472,7 @@ int launch_one(const EwLaunch& a) {
   if (vec && streamed > 0 && ntiles >= (uint64_t)sms * tma_min_tiles_per_sm()) {
     const int smem = kStages * kTileBytes * streamed + kStages * 8;
     if (!prepare_smem((const void*)ew_tma_kernel<F>, smem)) return DCF_ECUDA;
-    const uint64_t cap = (uint64_t)sms * tma_ctas_per_sm(streamed);
-    const uint64_t g = ntiles < cap ? ntiles : cap;
+    const uint64_t g = ntiles < (uint64_t)sms * kTmaCtasPerSm ? ntiles : (uint64_t)sms * kTmaCtasPerSm;
     ew_tma_kernel<F><<<(unsigned)g, kThreads, smem, a.stream>>>(p);
   } else if (vec) {
     const uint64_t items = a.n / (16 / sizeof(typename F::In));

@@ -67,16 +67,6 @@ int tma_min_tiles_per_sm() {
   return v;
 }
 
-int tma_ctas_per_sm(int streamed) {
-  static const int v = [] {
-    const char* e = getenv("DCF_TMA_CTAS_PER_SM");
-    const int x = e ? atoi(e) : 0;
-    return x > 0 && x <= 6 ? x : 0;
-  }();
-  if (v) return v;
-  return streamed == 1 ? kTmaCtasPerSmUnary : kTmaCtasPerSm;
-}
-
 // Which 2-byte transpose the status-reporting entry points use: the
 // bulk-tensor pipeline (DCF_TRANSPOSE=tma) or the plain-load kernel with a
 // register prefetch of the next tile (the default: faster on B200).
