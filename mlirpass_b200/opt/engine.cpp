@@ -318,7 +318,12 @@ void Engine::ensure_pinned() {
 void Engine::download(void* dst, const void* src, size_t bytes) {
   set_device();
   stats.d2h_bytes += bytes;
-  if (bytes < (1u << 20)) {
+  struct Timer {
+    double& acc;
+    std::chrono::steady_clock::time_point t = std::chrono::steady_clock::now();
+    ~Timer() { acc += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t).count(); }
+  } timer{stats.download_ms};
+  if (bytes < (1u << 20) || PinnedPool::get().owned(dst)) {  // small, or page-locked: straight there
     ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s_), "D2H");
     sync();
     return;

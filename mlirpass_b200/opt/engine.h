@@ -80,32 +80,32 @@ struct EngineStats {
 class Engine {
  public:
   explicit Engine(int device);
-  ~Engine();
-  int device() const { return dev_; }
+  virtual ~Engine();
+  virtual int device() const { return dev_; }
 
   // Run every request (all belong to this engine's device).  Throws on a
   // runtime error; a refused fold is an outcome, not an error.
-  void execute(const std::vector<FoldRequest*>& reqs);
+  virtual void execute(const std::vector<FoldRequest*>& reqs);
 
   // Make a constant resident on this device.
-  void to_device(DenseValue& v);
+  virtual void to_device(DenseValue& v);
   // Make its bytes available on the host (downloading if needed).
-  void to_host(DenseValue& v);
+  virtual void to_host(DenseValue& v);
   // The same for many constants with one synchronisation: their hex texts
   // (or host bytes) are packed back to back through the pinned slots into
   // one device arena and decoded there; results come back through the
   // slots the same way.
-  void to_device_all(const std::vector<DenseValue*>& vs);
-  void to_host_all(const std::vector<DenseValue*>& vs);
+  virtual void to_device_all(const std::vector<DenseValue*>& vs);
+  virtual void to_host_all(const std::vector<DenseValue*>& vs);
   // Uppercase hex digits of all its bytes (encoded on the device when
   // the value is there).
-  std::string hex_of(DenseValue& v);
-  uint64_t bits0_of(DenseValue& v);
+  virtual std::string hex_of(DenseValue& v);
+  virtual uint64_t bits0_of(DenseValue& v);
   // 64-bit hash of the bytes (dcf_hash_many_async; computed on upload and
   // for every fold result, so deduplication rarely launches anything).
-  uint64_t hash_of(DenseValue& v);
+  virtual uint64_t hash_of(DenseValue& v);
   // Whether every value equals the first (cached in v.all_equal).
-  bool all_equal(DenseValue& v);
+  virtual bool all_equal(DenseValue& v);
 
   EngineStats stats;
 
@@ -148,6 +148,47 @@ class Engine {
   void check(int rc, const char* what);
   void sync();
   dcf_status* statuses(size_t n);
+};
+
+// Bare `canonicalize` over several GPUs.  Every fold that canonicalize
+// runs element by element maps element i of its operands to element i of
+// its result, so a large constant is cut into contiguous element ranges,
+// range g living on GPU g, and each fold of such constants runs as one fold
+// per range, on all GPUs at once.  Through a chain of folds the ranges stay
+// aligned and no bytes cross GPUs; results come back to the host range by
+// range.  Small constants (under kMinElements) stay whole on the first GPU.
+//
+// A sharded constant keeps its ranges in DenseValue::parts.  Its hash is a
+// fixed combination of the ranges' hashes, so two constants of the same
+// type compare equal exactly when their ranges do; an all-equal range that
+// came back as one element hashes as its expansion.  The result of a fold
+// is one element when every range came back as the same single element,
+// which is when the kernel over the whole range would have said so.
+class ShardedEngine : public Engine {
+ public:
+  explicit ShardedEngine(std::vector<Engine*> subs);
+  static constexpr uint64_t kMinElements = 1u << 18;
+  static constexpr uint64_t kAlign = 4096;  // range boundaries, in elements
+  int device() const override { return subs_[0]->device(); }
+  void execute(const std::vector<FoldRequest*>& reqs) override;
+  void to_device(DenseValue& v) override;
+  void to_device_all(const std::vector<DenseValue*>& vs) override;
+  void to_host(DenseValue& v) override;
+  void to_host_all(const std::vector<DenseValue*>& vs) override;
+  std::string hex_of(DenseValue& v) override;
+  uint64_t bits0_of(DenseValue& v) override;
+  uint64_t hash_of(DenseValue& v) override;
+  bool all_equal(DenseValue& v) override;
+
+ private:
+  std::vector<Engine*> subs_;
+  bool shardable(const DenseValue& v) const;
+  uint64_t chunk(uint64_t n) const;
+  void split(DenseValue& v);
+  Engine* owner(const DenseValue& v) const;
+  uint64_t part_hash(const DenseValue& whole, size_t g);
+  // Run f(g) for every range g on its own host thread.
+  template <class F> void each(size_t parts, F&& f);
 };
 
 }  // namespace dco

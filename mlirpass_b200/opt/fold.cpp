@@ -1456,10 +1456,11 @@ void fetch_results(Module& m, std::vector<Engine*>& engines) {
   while (!stack.empty()) {
     Op* o = stack.back();
     stack.pop_back();
-    if (o->cst && o->cst->dev && o->cst->host.empty() && !o->cst_text) {
+    if (o->cst && (o->cst->dev || !o->cst->parts.empty()) && o->cst->host.empty() && !o->cst_text) {
       Engine* e = engines[0];
-      for (Engine* x : engines)
-        if (x->device() == o->cst->dev->device) e = x;
+      if (o->cst->dev && engines.size() > 1)
+        for (Engine* x : engines)
+          if (x->device() == o->cst->dev->device) e = x;
       per[e].push_back(o->cst.get());
     }
     for (Region* r : o->regions)

@@ -107,6 +107,10 @@ struct DenseValue {
   Bytes host;                // host bytes, empty when not on the host
   std::string_view hex;      // "HEX…" digits (no 0x), when parsed from text
   std::shared_ptr<DeviceBuf> dev;  // device bytes
+  // Element ranges on several GPUs (a sharded constant, ShardedEngine):
+  // contiguous, in order, each a DenseValue of its own (one element when
+  // that range is all equal).
+  std::vector<std::shared_ptr<DenseValue>> parts;
   int all_equal = -1;        // cached "every value equal" test: -1 unknown
   uint64_t hash = 0;         // dcf_hash_many_async of the bytes, when hashed
   bool hashed = false;

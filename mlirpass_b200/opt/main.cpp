@@ -41,8 +41,30 @@ struct Engines {
       own.push_back(std::make_unique<dco::Engine>(i));
       list.push_back(own.back().get());
     }
+    // DCF_OPT_RANGES_PER_GPU (default 1): element ranges per GPU for bare
+    // canonicalize, each run by an engine (stream) of its own.
+    const char* e = getenv("DCF_OPT_RANGES_PER_GPU");
+    const int k = e && atoi(e) > 0 ? atoi(e) : 1;
+    std::vector<dco::Engine*> subs(list);
+    for (int r = 1; r < k; r++)
+      for (int i = 0; i < n; i++) {
+        own.push_back(std::make_unique<dco::Engine>(i));
+        subs.push_back(own.back().get());
+      }
+    if (subs.size() > 1) sharded = std::make_unique<dco::ShardedEngine>(subs);
   }
+  // Bare `canonicalize` runs the whole module as one unit (the reference
+  // runs it on one thread); over several GPUs its large constants are split
+  // into element ranges, one per GPU.  Nested pipelines place whole
+  // functions on the GPUs instead.
+  std::vector<dco::Engine*> for_pipeline(const std::string& pipeline) {
+    size_t a = pipeline.find_first_not_of(" \t-");
+    if (sharded && a != std::string::npos && pipeline.compare(a, 12, "canonicalize") == 0) return {sharded.get()};
+    return list;
+  }
+  std::unique_ptr<dco::ShardedEngine> sharded;
   dco::Engine* of(const dco::DenseValue& v) {
+    if (sharded && !v.parts.empty()) return sharded.get();
     if (v.dev)
       for (auto* e : list)
         if (e->device() == v.dev->device) return e;
@@ -114,11 +136,12 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
     dco::Module& m = *mods.back();
     total.parse_ms += ms_since(t0);
     if (i == 0 && is_pinned(text))
-      for (auto* e : eng.list) e->set_pinned_source(text.data(), text.size());
+      for (auto& e : eng.own) e->set_pinned_source(text.data(), text.size());
     t0 = Clock::now();
     dco::PassStats ps;
-    dco::run_pipeline(m, pipeline, eng.list, &ps);
-    dco::fetch_results(m, eng.list);
+    std::vector<dco::Engine*> engines = eng.for_pipeline(pipeline);
+    dco::run_pipeline(m, pipeline, engines, &ps);
+    dco::fetch_results(m, engines);
     total.run_ms += ms_since(t0);
     total.folds += ps.folds;
     total.refused += ps.refused;
@@ -152,7 +175,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
   }
   out.p[out.n] = 0;
   total.print_ms += ms_since(t0);
-  for (auto* e : eng.list) {
+  for (auto& e : eng.own) {
     total.h2d_bytes += e->stats.h2d_bytes;
     total.d2h_bytes += e->stats.d2h_bytes;
     total.batches += e->stats.batches;

@@ -354,3 +354,64 @@ def test_math_folds_through_canonicalize(oracle):
              oracle.convert("absi", "i32", "i32", x).out, oracle.binary("ipowi", "i32", x, y).out]
     for i, (d, w) in enumerate(zip(got, want)):
         assert np.array_equal(full(d, n), w.astype(np.uint64)), i
+
+
+def _ranges_module():
+    # Constants of 2^19 elements: a float whose first half is all 1.0 (so a
+    # result range comes back as one element), one of all-equal values
+    # written out in full (a result that is a splat as a whole), an all-zero
+    # literal (addf gives back the first operand, which deduplicates against
+    # it), and two i32 constants for a two-result fold and a refusal.
+    rng = np.random.default_rng(7)
+    n = 1 << 19
+    F, I = f"tensor<{n}xf32>", f"tensor<{n}xi32>"
+    a = np.concatenate([np.full(n // 2, 1.0, np.float32), rng.standard_normal(n // 2).astype(np.float32)])
+    c = np.full(n, 2.0, np.float32)
+    z = np.zeros(n, np.float32)
+    x = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    y = rng.integers(1, 1 << 31, n, dtype=np.uint64).astype(np.uint32)
+    y0 = y.copy()
+    y0[n - 5] = 0                                       # divsi refuses in the last range
+    fm = "<{fastmath = #arith.fastmath<none>}>"
+    lines = [
+        f'    %a = "arith.constant"() <{{value = dense<"0x{_hex(a.view(np.uint32))}"> : {F}}}> : () -> {F}',
+        f'    %c = "arith.constant"() <{{value = dense<"0x{_hex(c.view(np.uint32))}"> : {F}}}> : () -> {F}',
+        f'    %z = "arith.constant"() <{{value = dense<"0x{_hex(z.view(np.uint32))}"> : {F}}}> : () -> {F}',
+        f'    %x = "arith.constant"() <{{value = dense<"0x{_hex(x)}"> : {I}}}> : () -> {I}',
+        f'    %y = "arith.constant"() <{{value = dense<"0x{_hex(y)}"> : {I}}}> : () -> {I}',
+        f'    %y0 = "arith.constant"() <{{value = dense<"0x{_hex(y0)}"> : {I}}}> : () -> {I}',
+        f'    %s = "arith.constant"() <{{value = dense<3.000000e+00> : {F}}}> : () -> {F}',
+        f'    %0 = "arith.mulf"(%a, %s) {fm} : ({F}, {F}) -> {F}',
+        f'    %1 = "arith.addf"(%c, %c) {fm} : ({F}, {F}) -> {F}',
+        f'    %2 = "arith.addf"(%a, %z) {fm} : ({F}, {F}) -> {F}',
+        f'    %3:2 = "arith.addui_extended"(%x, %y) : ({I}, {I}) -> ({I}, tensor<{n}xi1>)',
+        f'    %4 = "arith.divsi"(%x, %y0) : ({I}, {I}) -> {I}',
+        f'    %5 = "arith.subf"(%0, %a) {fm} : ({F}, {F}) -> {F}',
+    ]
+    tys = [F, F, F, I, f"tensor<{n}xi1>", I, F]
+    rets = ["%0", "%1", "%2", "%3#0", "%3#1", "%4", "%5"]
+    return ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({", ".join(tys)}), sym_name = "main"}}> ({{\n'
+            + "\n".join(lines) + f'\n    "func.return"({", ".join(rets)}) : ({", ".join(tys)}) -> ()\n'
+            '  }) : () -> ()\n}) : () -> ()\n')
+
+
+@pytest.mark.parametrize("gpus,ranges", [(1, 2), (1, 3), (2, 1), (4, 1), (8, 1), (2, 3)])
+def test_canonicalize_by_element_ranges_prints_the_same(gpus, ranges, monkeypatch):
+    # Bare canonicalize over several engines cuts large constants into
+    # element ranges; the printed module must not depend on it: the same
+    # folds, refusals, splat results and deduplications as one engine.
+    if _gpus() < gpus:
+        pytest.skip(f"needs {gpus} GPUs")
+    texts = [_ranges_module(), mlir_gen.config2_text(1024), mlir_gen.config3_text("i32", 1024, 512),
+             mlir_gen.config4_text(1 << 19, prerounded=True)]
+    want = [opt.run(t, "canonicalize", n_gpus=1) for t in texts]
+    monkeypatch.setenv("DCF_OPT_RANGES_PER_GPU", str(ranges))
+    for t, (one, s1) in zip(texts, want):
+        many, sn = opt.run(t, "canonicalize", n_gpus=gpus)
+        assert many == one
+        assert (sn["folds"], sn["refused"]) == (s1["folds"], s1["refused"])
+    out = want[0][0]
+    f = parse_funcs(out)["main"]
+    d = [f.defs.get(v) for v in f.ret.operands]
+    assert d[1].const.splat and d[5].name == "arith.divsi"
