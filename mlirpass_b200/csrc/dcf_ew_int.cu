@@ -13,13 +13,59 @@ template <int OP, int W> constexpr bool word_op() {
                                  OP == DCF_MINUI);
 }
 
+template <int OP, int W> constexpr bool checked_word_op() {
+  return (W == 8 || W == 16) && (OP == DCF_MULI || OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI ||
+                                 OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI);
+}
+
 template <int OP, int W> struct IOp {
   using In = typename IntW<W>::T;
   using Out = typename IntW<W>::T;
   static constexpr bool kBinary = true;
   static constexpr bool kWord = word_op<OP, W>();
-  // Four i8 (two i16) lanes per word: the video SIMD intrinsics wrap per
-  // lane, as the element closures do.
+  static constexpr bool kWordChecked = checked_word_op<OP, W>();
+  // Lane by lane in registers, with the refusals of all lanes found at
+  // once (the returned mask): a shift amount of the width or more, a zero
+  // divisor, and the signed minimum divided by -1; a refusing lane still
+  // gets some value, which is never used.  Quotients of 8- and 16-bit
+  // lanes come from one correctly rounded f32 division: for |x| < 2^24 its
+  // error is below the distance 1/|y| from x/y to the next integer, so
+  // truncating it gives the exact quotient.
+  __device__ static __forceinline__ uint32_t word_checked(uint32_t a, uint32_t b, uint32_t& o) {
+    constexpr uint32_t M = (1u << W) - 1;
+    uint32_t bad = 0;
+    if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI)
+      bad = W == 8 ? __vcmpgeu4(b, 0x08080808u) : __vcmpgeu2(b, 0x00100010u);
+    if constexpr (OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI)
+      bad = W == 8 ? __vcmpeq4(b, 0u) : __vcmpeq2(b, 0u);
+    if constexpr (OP == DCF_DIVSI)
+      bad |= W == 8 ? (__vcmpeq4(a, 0x80808080u) & __vcmpeq4(b, 0xFFFFFFFFu))
+                    : (__vcmpeq2(a, 0x80008000u) & __vcmpeq2(b, 0xFFFFFFFFu));
+    uint32_t r = 0;
+#pragma unroll
+    for (int k = 0; k < 32 / W; k++) {
+      const uint32_t x = (a >> (W * k)) & M;
+      uint32_t y = (b >> (W * k)) & M;
+      if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI) y &= W - 1;
+      if constexpr (OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI) y = y ? y : 1;
+      const int32_t sx = (int32_t)(x << (32 - W)) >> (32 - W), sy = (int32_t)(y << (32 - W)) >> (32 - W);
+      uint32_t z;
+      if constexpr (OP == DCF_MULI) z = x * y;
+      else if constexpr (OP == DCF_SHLI) z = x << y;
+      else if constexpr (OP == DCF_SHRUI) z = x >> y;
+      else if constexpr (OP == DCF_SHRSI) z = (uint32_t)(sx >> y);
+      else if constexpr (OP == DCF_DIVUI || OP == DCF_REMUI) {
+        const uint32_t q = (uint32_t)truncf(__fdiv_rn((float)x, (float)y));
+        z = OP == DCF_DIVUI ? q : x - q * y;
+      } else {
+        const int32_t q = (int32_t)truncf(__fdiv_rn((float)sx, (float)sy));
+        z = (uint32_t)(OP == DCF_DIVSI ? q : sx - q * sy);
+      }
+      r |= (z & M) << (W * k);
+    }
+    o = r;
+    return bad;
+  }
   __device__ static __forceinline__ uint32_t word(uint32_t a, uint32_t b) {
     if constexpr (OP == DCF_ANDI) return a & b;
     else if constexpr (OP == DCF_ORI) return a | b;

@@ -121,6 +121,15 @@ __device__ __forceinline__ void load_chunk(const typename F::In* __restrict__ l,
 template <class F, class = void> struct HasWord : std::false_type {};
 template <class F> struct HasWord<F, std::void_t<decltype(F::kWord)>> : std::bool_constant<F::kWord> {};
 
+// Functors whose op may refuse can define `kWordChecked` and
+// `word_checked(a, b, o)`: the op on the packed lanes of one word, returning
+// a mask with every bit of each refusing lane set (0: none refuses).  The
+// lowest refusing lane gives the element index; no element path is taken,
+// so a warp with a refusing lane does not diverge.
+template <class F, class = void> struct HasCheckedWord : std::false_type {};
+template <class F>
+struct HasCheckedWord<F, std::void_t<decltype(F::kWordChecked)>> : std::bool_constant<F::kWordChecked> {};
+
 template <class T> __device__ __forceinline__ uint32_t replicate32(T v) {
   if constexpr (sizeof(T) == 1) return (uint32_t)(uint8_t)v * 0x01010101u;
   else return (uint32_t)(uint16_t)v * 0x00010001u;
@@ -142,6 +151,25 @@ __device__ __forceinline__ void fold_chunk(typename F::Out* __restrict__ o, uint
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       rw[k] = F::word(aw[k], bw[k]);
+      nonsplat |= rw[k] != o0w;
+    }
+    *(uint4*)(o + c * VEC) = r;
+    return;
+  }
+  if constexpr (HasCheckedWord<F>::value && VEC * sizeof(In) == 16 && sizeof(Out) == sizeof(In)) {
+    const uint32_t* aw = (const uint32_t*)av;
+    const uint32_t* bw = (const uint32_t*)bv;
+    uint4 r;
+    uint32_t* rw = (uint32_t*)&r;
+    const uint32_t o0w = replicate32(o0);
+    constexpr int kLanes = int(4 / sizeof(In));
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t m = F::word_checked(aw[k], bw[k], rw[k]);
+      if (m) {
+        const uint64_t idx = base + c * VEC + k * kLanes + (__ffs((int)m) - 1) / (8 * int(sizeof(In)));
+        my_fail = idx < my_fail ? idx : my_fail;
+      }
       nonsplat |= rw[k] != o0w;
     }
     *(uint4*)(o + c * VEC) = r;

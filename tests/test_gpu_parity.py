@@ -329,3 +329,31 @@ def test_bulk_copy_path_vs_oracle(kind, op, dt, extra, dcf, oracle):
         if op == "fptosi":
             x = oracle.convert("sitofp", "i16", "f64", rbits("i16", n, 76)).out
         same(dcf.convert(op, dt, extra, x), oracle.convert(op, dt, extra, x), n)
+
+
+@pytest.mark.parametrize("op", ["muli", "shli", "shrui", "shrsi", "divsi", "divui", "remsi", "remui"])
+def test_i8_lanes_exhaustive_and_i16_edges(op, dcf, oracle):
+    # Every i8 pair (the lane-wise word path packs four per word and divides
+    # through f32), then i16 pairs around the largest dividends and the
+    # smallest divisors, where an inexact quotient would first show.
+    x, y = np.meshgrid(np.arange(256, dtype=np.uint8), np.arange(256, dtype=np.uint8))
+    a, b = x.ravel().copy(), y.ravel().copy()
+    if op.startswith("sh"):
+        b %= np.uint8(8)
+    if op in ("divsi", "divui", "remsi", "remui"):
+        b = np.where(b == 0, np.uint8(1), b)
+        if op == "divsi":
+            b = np.where((a == 0x80) & (b == 0xFF), np.uint8(1), b)
+    same(dcf.binary(op, "i8", a, b), oracle.binary(op, "i8", a, b), a.size)
+    # and with the refusals left in: the lowest refusing element
+    a2, b2 = x.ravel().copy(), y.ravel().copy()
+    same(dcf.binary(op, "i8", a2, b2), oracle.binary(op, "i8", a2, b2), a2.size)
+    big = np.concatenate([np.arange(65536 - 512, 65536), np.arange(0, 512), np.arange(32768 - 256, 32768 + 256)])
+    small = np.concatenate([np.arange(1, 300), np.arange(65536 - 300, 65536)])
+    xa, yb = np.meshgrid(big.astype(np.uint16), small.astype(np.uint16))
+    a, b = xa.ravel().copy(), yb.ravel().copy()
+    if op.startswith("sh"):
+        b %= np.uint16(16)
+    if op == "divsi":
+        b = np.where((a == 0x8000) & (b == 0xFFFF), np.uint16(1), b)
+    same(dcf.binary(op, "i16", a, b), oracle.binary(op, "i16", a, b), a.size)
