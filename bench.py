@@ -494,7 +494,8 @@ def run_kernels(args):
 
 def run_profile_kernels(args):
     """One launch per round (two rounds) of the kernels profiled with ncu:
-    truncf f32->bf16, fptosi f32->i32, addi i8, the batched addf of 1024
+    truncf f32->bf16, fptosi f32->i32, addi / divsi / shli i8 (the last two
+    lane-wise with a refusal mask), the batched addf of 1024
     256x256 functions, and the 16384x16384 bf16 transpose (bulk-tensor and
     plain-load kernels).  Operands are device-resident and larger than L2;
     nothing is timed here (the numbers come from the profiler)."""
@@ -512,6 +513,8 @@ def run_profile_kernels(args):
     xi = x.clamp(-2e9, 2e9)
     a8 = torch.randint(-128, 127, (n,), dtype=torch.int8, device=dev, generator=g)
     b8 = torch.randint(-128, 127, (n,), dtype=torch.int8, device=dev, generator=g)
+    d8 = torch.where(b8 == 0, torch.ones_like(b8), b8)                  # nonzero divisors
+    s8 = b8 & 7                                                          # in-range shift amounts
     w = torch.randint(-30000, 30000, (16384, 16384), dtype=torch.int16, device=dev, generator=g)
     o16 = torch.empty(n, dtype=torch.int16, device=dev)
     o32 = torch.empty(n, dtype=torch.int32, device=dev)
@@ -530,6 +533,10 @@ def run_profile_kernels(args):
         dcf.convert_async("fptosi", "f32", "i32", xi, o32, st)
         dcf.status_reset(st)
         dcf.binary_async("addi", "i8", a8, b8, o8, st)
+        dcf.status_reset(st)
+        dcf.binary_async("divsi", "i8", a8, d8, o8, st)
+        dcf.status_reset(st)
+        dcf.binary_async("shli", "i8", a8, s8, o8, st)
         dcf.status_reset(st)
         dcf.permute_async(2, (16384, 16384), (1, 0), w, wo, st)
         dcf.transpose2d_async(2, 16384, 16384, w, wo)
