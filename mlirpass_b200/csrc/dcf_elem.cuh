@@ -301,6 +301,20 @@ template <class L> __device__ __forceinline__ int fcompare(uint64_t a, uint64_t 
   }
 }
 
+// Total order of the non-NaN values of a sign-magnitude layout as a signed
+// integer: -0 just below +0, negatives by magnitude downwards.  It is the
+// numeric order with maximumf's -0 < +0 (canonicalize.rs:132-150), so one
+// integer compare decides min / max.
+template <class L> __device__ __forceinline__ auto order_key(uint64_t x) {
+  if constexpr (L::B == 8) {
+    const int64_t m = (int64_t)(x & (L::SIGN - 1));
+    return (x & L::SIGN) ? -m - 1 : m;
+  } else {
+    const int32_t m = (int32_t)(x & (L::SIGN - 1));
+    return (x & L::SIGN) ? -m - 1 : m;
+  }
+}
+
 template <class L, bool MAX, bool NANWINS>
 __device__ __forceinline__ uint64_t minmax(uint64_t a, uint64_t b) {
   const bool an = is_nan<L>(a), bn = is_nan<L>(b);
@@ -310,10 +324,9 @@ __device__ __forceinline__ uint64_t minmax(uint64_t a, uint64_t b) {
     if (bn && !(b & L::QUIET)) return b | L::QUIET;
     return an ? b : a;
   }
-  if (is_zero<L>(a) && is_zero<L>(b) && sign_of<L>(a) != sign_of<L>(b))
-    return (sign_of<L>(a) == MAX) ? b : a;
-  if (MAX) return fcompare<L>(a, b) == -1 ? b : a;
-  return fcompare<L>(b, a) == -1 ? b : a;
+  const auto ka = order_key<L>(a), kb = order_key<L>(b);
+  if (MAX) return ka < kb ? b : a;
+  return kb < ka ? b : a;
 }
 
 template <class L> __device__ __forceinline__ uint8_t cmpf(int pred, uint64_t a, uint64_t b) {
