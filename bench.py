@@ -411,7 +411,8 @@ def run_kernels(args):
     st = torch.empty(2, dtype=torch.int64, device=dev)
     T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
-    def timeit(launch, nbytes, label, reps=None):
+    def timeit(launch, nbytes, label, reps=None, in_bytes=None):
+        # A fold that ends "not folded" counts its input bytes only.
         reps = reps or args.steps
         times = []
         for r in range(args.warmup + reps):
@@ -425,9 +426,12 @@ def run_kernels(args):
             if r >= args.warmup:
                 times.append(e0.elapsed_time(e1))
         ms = statistics.median(times)
+        folded = dcf.status_read(st).folded
+        if not folded and in_bytes is not None:
+            nbytes = in_bytes
         gbs = nbytes / (ms * 1e-3) / 1e9
         line = {"workload": label[0], "fold": label[1], "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
-                "frac": round(gbs / peak, 3), "bytes": nbytes}
+                "frac": round(gbs / peak, 3), "bytes": nbytes, "folded": bool(folded)}
         print(json.dumps(line), flush=True)
 
     # config 1 / 2 (f32 binary)
@@ -445,7 +449,7 @@ def run_kernels(args):
         for op, l, r in (("addi", X, Y), ("muli", X, Y), ("subi", X, Y), ("andi", X, Y), ("xori", X, Y),
                          ("shli", X, S), ("divsi", Xd, Yd), ("remsi", Xd, Yd)):
             timeit(lambda op=op, l=l, r=r: dcf.binary_async(op, dt, l, r, o, st), 3 * es * X.numel(),
-                   (f"config3 8192x2048 {dt}", op))
+                   (f"config3 8192x2048 {dt}", op), in_bytes=2 * es * X.numel())
     # config 4 (conversions)
     c = W.config4()
     cp = W.config4(prerounded=True)
@@ -454,12 +458,12 @@ def run_kernels(args):
     o16 = torch.empty(n, dtype=torch.int16, device=dev)
     o32 = torch.empty(n, dtype=torch.int32, device=dev)
     o8 = torch.empty(n, dtype=torch.uint8, device=dev)
-    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->bf16 (refuses)"))
-    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", xr, o16, st), 6 * n, ("config4b 16M", "truncf f32->bf16"))
-    timeit(lambda: dcf.convert_async("truncf", "f32", "f16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->f16 (refuses)"))
-    timeit(lambda: dcf.convert_async("extf", "bf16", "f32", o16, o32, st), 6 * n, ("config4b 16M", "extf bf16->f32"))
-    timeit(lambda: dcf.convert_async("fptosi", "f32", "i32", inr, o32, st), 8 * n, ("config4 16M", "fptosi f32->i32"))
-    timeit(lambda: dcf.convert_async("sitofp", "i32", "f32", ints, o32, st), 8 * n, ("config4 16M", "sitofp i32->f32"))
+    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->bf16 (refuses)"), in_bytes=4 * n)
+    timeit(lambda: dcf.convert_async("truncf", "f32", "bf16", xr, o16, st), 6 * n, ("config4b 16M", "truncf f32->bf16"), in_bytes=4 * n)
+    timeit(lambda: dcf.convert_async("truncf", "f32", "f16", x, o16, st), 6 * n, ("config4 16M", "truncf f32->f16 (refuses)"), in_bytes=4 * n)
+    timeit(lambda: dcf.convert_async("extf", "bf16", "f32", o16, o32, st), 6 * n, ("config4b 16M", "extf bf16->f32"), in_bytes=2 * n)
+    timeit(lambda: dcf.convert_async("fptosi", "f32", "i32", inr, o32, st), 8 * n, ("config4 16M", "fptosi f32->i32"), in_bytes=4 * n)
+    timeit(lambda: dcf.convert_async("sitofp", "i32", "f32", ints, o32, st), 8 * n, ("config4 16M", "sitofp i32->f32"), in_bytes=4 * n)
     timeit(lambda: dcf.binary_async("cmpf", "f32", x, inr, o8, st, flags=4 << 8), 9 * n,
            ("config4 16M", "cmpf olt (kernel only; dense cmpf is not folded)"))
     # config 5: 4096 functions per step, batched; and the 16384^2 bf16 transpose
