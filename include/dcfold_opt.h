@@ -45,8 +45,8 @@ typedef struct dcf_opt_stats {
  * (--mlir-print-debuginfo) locations are printed, without it op and block
  * argument locations and `#loc` aliases are dropped.  Alias definitions
  * that the printed module does not use are dropped.  On success *out is a
- * malloc'ed
- * printed module (free with dcf_opt_free) and the return value is 0;
+ * buffer holding the
+ * printed module (give it back with dcf_opt_free) and the return value is 0;
  * otherwise a negative code and dcf_opt_last_error() says why. */
 #define DCF_OPT_SPLIT_INPUT_FILE 1
 #define DCF_OPT_LOCAL_SCOPE 2
@@ -55,6 +55,8 @@ typedef struct dcf_opt_stats {
 int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int flags,
                 char** out, size_t* out_len, dcf_opt_stats* stats);
 
+/* Give back an output buffer.  The library keeps the last buffer given
+ * back, with its pages mapped, for a later run whose output fits it. */
 void dcf_opt_free(char* p);
 
 const char* dcf_opt_last_error(void);

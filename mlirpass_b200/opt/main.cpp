@@ -8,6 +8,7 @@
 #include <fstream>
 #include <iostream>
 #include <memory>
+#include <mutex>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -115,7 +116,45 @@ std::vector<std::string_view> split_chunks(std::string_view text, bool split) {
   return out;
 }
 
-// The printed result, malloc'd (handed to the C API's caller as is).
+// Output buffers.  Printing a large module into fresh memory spends much
+// of its time in page faults, so the last buffer given back with
+// dcf_opt_free is kept (its pages stay mapped) and serves the next run
+// whose output fits in it without wasting more than half of it.  Each
+// buffer carries its capacity in a 64-byte header.
+constexpr size_t kOutHeader = 64;
+std::mutex g_out_mu;
+char* g_out_keep = nullptr;  // a header address, or null
+
+size_t out_cap(char* hdr) { return *(size_t*)hdr; }
+
+char* out_alloc(size_t n) {
+  {
+    std::lock_guard<std::mutex> g(g_out_mu);
+    if (g_out_keep && out_cap(g_out_keep) >= n && out_cap(g_out_keep) / 2 <= n) {
+      char* h = g_out_keep;
+      g_out_keep = nullptr;
+      return h + kOutHeader;
+    }
+  }
+  char* h = (char*)malloc(n + kOutHeader);
+  if (!h) return nullptr;
+  *(size_t*)h = n;
+  return h + kOutHeader;
+}
+
+void out_free(char* p) {
+  if (!p) return;
+  char* h = p - kOutHeader;
+  std::lock_guard<std::mutex> g(g_out_mu);
+  if (g_out_keep && out_cap(g_out_keep) >= out_cap(h)) {
+    free(h);
+    return;
+  }
+  free(g_out_keep);
+  g_out_keep = h;
+}
+
+// The printed result (handed to the C API's caller as is; dcf_opt_free).
 struct Output {
   char* p = nullptr;
   size_t n = 0;
@@ -161,7 +200,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
   static const char sep[] = "// -----\n";
   Output out;
   for (size_t i = 0; i < parts.size(); i++) out.n += parts[i].size() + tail + (i ? sizeof sep - 1 : 0);
-  out.p = (char*)malloc(out.n + 1);
+  out.p = out_alloc(out.n + 1);
   if (!out.p) throw std::runtime_error("out of memory for the printed module");
   size_t at = 0;
   for (size_t i = 0; i < parts.size(); i++) {
@@ -206,7 +245,7 @@ extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, i
   }
 }
 
-extern "C" void dcf_opt_free(char* p) { free(p); }
+extern "C" void dcf_opt_free(char* p) { out_free(p); }
 
 extern "C" const char* dcf_opt_last_error(void) { return g_opt_err.c_str(); }
 
@@ -268,7 +307,7 @@ int main(int argc, char** argv) {
       std::ofstream f(output, std::ios::binary);
       f.write(r.p, (std::streamsize)r.n);
     }
-    free(r.p);
+    out_free(r.p);
   } catch (const std::exception& e) {
     fprintf(stderr, "dcfold-opt: %s\n", e.what());
     return 1;
