@@ -242,3 +242,19 @@ def test_math_element_folds_need_a_gpu():
     body = const("%a", C4, T) + '\n    %0 = "math.ceil"(%a) <{fastmath = #arith.fastmath<none>}> : (tensor<4xf32>) -> tensor<4xf32>'
     with pytest.raises(opt.OptError, match="needs a GPU"):
         run(module(body, "%0", T))
+
+
+def test_output_buffers_given_back_are_reused_safely():
+    # dcf_opt_free keeps the last buffer for a later run whose output fits
+    # it; outputs of alternating sizes must come out whole each time.
+    from mlirpass_b200 import mlir_gen
+    big = mlir_gen.config5_text(funcs=8, side=32, weight_side=0)
+    small = module(const("%0", C4, T), "%0", T)
+    want = {}
+    for text in (big, small, big, small, small, big):
+        out, _ = opt.run(text, "builtin.module(func.func())", n_gpus=0, as_array=True)
+        got = out.tobytes()
+        del out
+        want.setdefault(text, got)
+        assert got == want[text]
+        assert got.endswith(b") : () -> ()\n\n")
