@@ -22,6 +22,8 @@ BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libdcfold.so")
 ORACLE_SRC = os.path.join(ROOT, "oracle", "dcf_oracle.c")
 ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "libdcforacle.so")
+GEN_SRC = os.path.join(PKG, "gen", "dcf_gen.c")
+GEN_LIB = os.path.join(PKG, "libdcfgen.so")
 
 # The float and conversion kernel families are split by layout so that the
 # (template-heavy) translation units compile in parallel.
@@ -133,12 +135,26 @@ def build_oracle(force: bool = False) -> str:
     return ORACLE_LIB
 
 
+def build_gen(force: bool = False) -> str:
+    """The host generator of the synthetic workloads (libdcfgen.so)."""
+    if force or _stale(GEN_LIB, [GEN_SRC]):
+        cc = os.environ.get("CC", "gcc")
+        cmd = [cc, "-O3", "-std=c11", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math", "-Wall",
+               "-o", GEN_LIB, GEN_SRC, "-lpthread"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode:
+            sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+            raise RuntimeError("build of libdcfgen.so failed")
+    return GEN_LIB
+
+
 def main(argv: list[str]) -> None:
     force = "--force" in argv
     if "--oracle" not in argv:
         print(build_lib(verbose="-v" in argv, force=force))
         for t in build_opt(force=force):
             print(t)
+        print(build_gen(force=force))
     if "--lib" not in argv:
         print(build_oracle(force=force))
 

@@ -16,10 +16,23 @@
 //   - every call shares the one array per device and leaves its contents
 //     behind; each call re-initialises what it uses (descriptors written,
 //     statuses filled with 0xFF) before its kernels read them;
-//   - calls whose work overlaps on a GPU (two host threads, or two streams,
-//     at once) race on the array: serialise them;
+//   - work that overlaps on a GPU and uses the array races on it.  The
+//     library therefore holds a per-device lock from the first copy into the
+//     array to the synchronisation that ends the call, so calls made from
+//     several host threads at once (the pass driver's engines that share a
+//     GPU, say) take turns instead of overwriting each other's descriptors;
 //   - the first call on each device looks up the array's device address
-//     with cudaGetSymbolAddress, with that device current.
+//     with cudaGetSymbolAddress, with that device current.  Make that first
+//     call before any stream capture on that device;
+//   - the host-side copies of the descriptors and statuses live in static
+//     per-device arrays (guarded by the same lock), not on the caller's
+//     stack, so the call needs only a few hundred bytes of stack;
+//   - every operand and result pointer must be device memory of one device,
+//     and the bytes a job touches must lie inside that pointer's allocation
+//     where the driver can report it (cuMemGetAddressRange); anything else
+//     is rejected with DCF_EINVAL before any copy or launch;
+//   - the caller's current device is the same on return as on entry.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -33,6 +46,7 @@ namespace dcf {
 constexpr size_t kNoAllocMaxJobs = 1024;
 constexpr size_t kNoAllocDescBytes = kNoAllocMaxJobs * sizeof(BatchDesc);
 constexpr size_t kNoAllocBytes = kNoAllocDescBytes + kNoAllocMaxJobs * sizeof(dcf_status);
+constexpr int kNoAllocMaxDevices = 64;
 
 // The scratch: descriptors [0, kNoAllocDescBytes), then the job statuses.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
@@ -42,15 +56,21 @@ namespace {
 // Errors go to the same per-thread text that dcf_last_error() returns.
 int noalloc_fail(int code, const char* msg) { return record_error(code, msg); }
 
-// Device address of g_noalloc_scratch on each device (host code cannot use
-// the symbol's host-side name as a device pointer).
-std::mutex g_sym_mu;
-void* g_sym_addr[64] = {nullptr};
+// Per device: the lock that serialises calls, the array's device address
+// (host code cannot use the symbol's host-side name as a device pointer),
+// and the host-side images of the descriptors and statuses.
+struct DeviceSlot {
+  std::mutex mu;
+  unsigned char* scratch = nullptr;
+  BatchDesc desc[kNoAllocMaxJobs];
+  dcf_status status[kNoAllocMaxJobs];
+  uint32_t order[kNoAllocMaxJobs];
+};
+DeviceSlot g_slots[kNoAllocMaxDevices];
 
-int scratch_on(int dev, unsigned char** out) {
-  if (dev < 0 || dev >= 64) return noalloc_fail(DCF_EINVAL, "device index out of range");
-  std::lock_guard<std::mutex> g(g_sym_mu);
-  if (!g_sym_addr[dev]) {
+// Called with the slot's lock held and its device current.
+int scratch_on(DeviceSlot& slot) {
+  if (!slot.scratch) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
@@ -58,15 +78,61 @@ int scratch_on(int dev, unsigned char** out) {
       snprintf(buf, sizeof buf, "cudaGetSymbolAddress(g_noalloc_scratch) failed: %s", cudaGetErrorString(e));
       return noalloc_fail(DCF_ECUDA, buf);
     }
-    g_sym_addr[dev] = p;
+    slot.scratch = (unsigned char*)p;
   }
-  *out = (unsigned char*)g_sym_addr[dev];
   return DCF_OK;
 }
 
-bool binary_op(uint32_t op) { return op_binary((int)op); }
+// cuMemGetAddressRange through the runtime's driver entry point (no link
+// against libcuda).  Null when the driver does not offer it.
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return (AddressRangeFn)p;
+    return (AddressRangeFn) nullptr;
+  }();
+  return fn;
+}
 
-bool convert_op(uint32_t op) { return op_convert((int)op); }
+// Whether [p, p + bytes) is device memory of one device; that device goes
+// to *dev.  When the driver reports the allocation around p, the range
+// must lie inside it.
+bool device_range(const void* p, uint64_t bytes, int* dev) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (at.type != cudaMemoryTypeDevice) return false;
+  *dev = at.device;
+  if (AddressRangeFn fn = address_range_fn()) {
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)(uintptr_t)p) == CUDA_SUCCESS) {
+      const uint64_t off = (uint64_t)((uintptr_t)p - (uintptr_t)base);
+      if (off > size || bytes > size - off) return false;
+    }
+  }
+  return true;
+}
+
+// Restores the caller's current device on every return path.
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      cudaGetLastError();
+      prev = -1;
+    }
+  }
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 }  // namespace
 
@@ -79,18 +145,33 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
   if (!jobs) return noalloc_fail(DCF_EINVAL, "null job list");
   if (n_jobs > kNoAllocMaxJobs)
     return noalloc_fail(DCF_EINVAL, "dcf_batch_noalloc takes at most 1024 jobs per call; split the list");
-  // Validate every job before touching the device.
+  // The device comes from the first job's result buffer; it is made current
+  // before the other checks, so that the driver can report allocation
+  // extents.
   int dev = -1;
+  for (size_t i = 0; i < n_jobs && dev < 0; i++) {
+    if (!jobs[i].n || !jobs[i].out) continue;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, jobs[i].out) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return noalloc_fail(DCF_EINVAL, "dcf_batch_noalloc needs device buffers that hold each job's operands and result");
+    }
+    dev = at.device;
+  }
+  if (dev >= kNoAllocMaxDevices) return noalloc_fail(DCF_EINVAL, "device index out of range");
+  DeviceRestore restore;
+  if (dev >= 0 && cudaSetDevice(dev) != cudaSuccess) return noalloc_fail(DCF_ECUDA, "cudaSetDevice failed");
+  // Validate every job before any copy or launch.
   for (size_t i = 0; i < n_jobs; i++) {
     dcf_job& j = jobs[i];
     memset(&j.result, 0, sizeof j.result);
     j.result.first_fail_index = UINT64_MAX;
-    const bool bin = binary_op(j.op);
+    const bool bin = op_binary((int)j.op);
     bool ok;
     if (bin) {
       ok = op_float_binary((int)j.op) ? is_float(j.dtype) : is_int(j.dtype);
       j.out_dtype = op_bool_result((int)j.op) ? DCF_I1 : j.dtype;
-    } else if (convert_op(j.op)) {
+    } else if (op_convert((int)j.op)) {
       ok = convert_types_ok((int)j.op, is_float(j.dtype), is_int(j.dtype), is_float(j.out_dtype), is_int(j.out_dtype),
                             (int)j.dtype, (int)j.out_dtype);
     } else if (j.op == DCF_RECIPROCAL) {
@@ -106,30 +187,33 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
       continue;
     }
     if (!j.lhs || !j.out || (bin && !j.rhs)) return noalloc_fail(DCF_EINVAL, "a job has a null buffer");
-    cudaPointerAttributes at;
-    if (cudaPointerGetAttributes(&at, j.out) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
-      cudaGetLastError();
-      return noalloc_fail(DCF_EINVAL, "dcf_batch_noalloc needs device buffers");
-    }
-    if (dev < 0) dev = at.device;
-    else if (dev != at.device) return noalloc_fail(DCF_EINVAL, "all jobs of one call must be on one device");
+    const uint64_t es = dtype_size((int)j.dtype), oes = dtype_size((int)j.out_dtype);
+    if (j.n > (UINT64_MAX >> 4)) return noalloc_fail(DCF_EINVAL, "a job's element count is too large");
+    int d_out = -1, d_l = -1, d_r = -1;
+    if (!device_range(j.out, j.n * oes, &d_out) || !device_range(j.lhs, j.lhs_splat ? es : j.n * es, &d_l) ||
+        (bin && !device_range(j.rhs, j.rhs_splat ? es : j.n * es, &d_r)))
+      return noalloc_fail(DCF_EINVAL,
+                          "dcf_batch_noalloc needs device buffers that hold each job's operands and result");
+    if (d_out != dev || d_l != dev || (bin && d_r != dev))
+      return noalloc_fail(DCF_EINVAL, "all operands and results of one call must be on one device");
   }
   if (dev < 0) return DCF_OK;
-  if (cudaSetDevice(dev) != cudaSuccess) return noalloc_fail(DCF_ECUDA, "cudaSetDevice failed");
-  unsigned char* scratch = nullptr;
-  if (int rc = scratch_on(dev, &scratch)) return rc;
+  DeviceSlot& slot = g_slots[dev];
+  std::lock_guard<std::mutex> lock(slot.mu);
+  if (int rc = scratch_on(slot)) return rc;
+  unsigned char* scratch = slot.scratch;
   BatchDesc* ddesc = (BatchDesc*)scratch;
   dcf_status* dst = (dcf_status*)(scratch + kNoAllocDescBytes);
   cudaStream_t s = (cudaStream_t)stream;
+  BatchDesc* hdesc = slot.desc;
+  dcf_status* hst = slot.status;
+  uint32_t* order = slot.order;
 
-  // Descriptors are built on the stack (no heap either) and copied into the
-  // scratch array in one transfer; statuses are reset to 0xFF there.
-  BatchDesc hdesc[kNoAllocMaxJobs];
-  dcf_status hst[kNoAllocMaxJobs];
-  size_t order[kNoAllocMaxJobs];
+  // Descriptors are built in the device's static host image and copied into
+  // the scratch array in one transfer; statuses are reset to 0xFF there.
   size_t m = 0;
   for (size_t i = 0; i < n_jobs; i++)
-    if (jobs[i].n) order[m++] = i;
+    if (jobs[i].n) order[m++] = (uint32_t)i;
   // Group jobs of one (op, dtype, out_dtype, flags) next to each other:
   // insertion sort keeps this allocation-free.
   auto key_less = [&](size_t a, size_t b) {
@@ -141,20 +225,21 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
   };
   for (size_t i = 1; i < m; i++)
     for (size_t k = i; k > 0 && key_less(order[k], order[k - 1]); k--) {
-      const size_t t = order[k];
+      const uint32_t t = order[k];
       order[k] = order[k - 1];
       order[k - 1] = t;
     }
   for (size_t t = 0; t < m; t++) {
     const dcf_job& j = jobs[order[t]];
-    const bool bin = binary_op(j.op);
+    const bool bin = op_binary((int)j.op);
     hdesc[t] = BatchDesc{j.lhs, bin ? j.rhs : nullptr, j.out, j.n, j.lhs_splat, bin ? j.rhs_splat : 0, dst + t};
   }
   cudaError_t e = cudaMemcpyAsync(ddesc, hdesc, m * sizeof(BatchDesc), cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(dst, 0xFF, m * sizeof(dcf_status), s);
   if (e != cudaSuccess) return noalloc_fail(DCF_ECUDA, cudaGetErrorString(e));
   size_t g0 = 0;
-  while (g0 < m) {
+  int rc = DCF_OK;
+  while (g0 < m && rc == DCF_OK) {
     size_t g1 = g0 + 1;
     while (g1 < m && !key_less(order[g0], order[g1]) && !key_less(order[g1], order[g0])) g1++;
     const dcf_job& j0 = jobs[order[g0]];
@@ -174,13 +259,17 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
     a.stream = s;
     // The launcher picks the vector kernel from these pointers' alignment.
     a.l = aligned ? (const void*)scratch : (const void*)(scratch + 1);
-    a.r = binary_op(j0.op) ? a.l : nullptr;
+    a.r = op_binary((int)j0.op) ? a.l : nullptr;
     a.o = (void*)a.l;
-    if (launch_ew(a) != DCF_OK) return noalloc_fail(DCF_ECUDA, cudaGetErrorString(cudaGetLastError()));
+    if (launch_ew(a) != DCF_OK) rc = noalloc_fail(DCF_ECUDA, cudaGetErrorString(cudaGetLastError()));
     g0 = g1;
   }
+  // Read the statuses back and wait, also after a failed launch, so that no
+  // work of this call is still using the array when the lock is released.
   e = cudaMemcpyAsync(hst, dst, m * sizeof(dcf_status), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  const cudaError_t es = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = es;
+  if (rc != DCF_OK) return rc;
   if (e != cudaSuccess) return noalloc_fail(DCF_ECUDA, cudaGetErrorString(e));
   for (size_t t = 0; t < m; t++) {
     dcf_job& j = jobs[order[t]];

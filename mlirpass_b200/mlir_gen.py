@@ -1,6 +1,10 @@
 """MLIR text (generic form, as mlir-opt prints it) for the five fold
 configurations: dense constants as `dense<"0x…">` hex literals (uppercase,
-little-endian raw bytes), one function per unit."""
+little-endian raw bytes), one function per unit.
+
+configN_text returns a str; configN_module returns the same text as a Text
+whose tobytes() builds it in one bytearray (the full-size modules are
+0.5-5.4 GB, where every extra copy of a str costs seconds)."""
 from __future__ import annotations
 
 import numpy as np
@@ -11,13 +15,51 @@ ELEM = {np.dtype(np.float32): "f32", np.dtype(np.uint16): "bf16"}
 
 
 def hexlit(a: np.ndarray) -> str:
-    return '"0x' + np.ascontiguousarray(a).tobytes().hex().upper() + '"'
+    return '"0x' + W.hex_upper(a) + '"'
+
+
+class Text:
+    """Module text as a list of parts: small strings, and arrays whose
+    uppercase hex is written straight into the final buffer (one pass over
+    the memory for literals of hundreds of MB)."""
+
+    def __init__(self, parts=None):
+        self.parts = parts or []
+
+    def __add__(self, other):
+        return Text(self.parts + (other.parts if isinstance(other, Text) else [other]))
+
+    def __radd__(self, other):
+        return Text([other] + self.parts)
+
+    def tobytes(self) -> bytearray:
+        import ctypes
+        enc = [p.encode() if isinstance(p, str) else np.ascontiguousarray(p).reshape(-1).view(np.uint8)
+               for p in self.parts]
+        total = sum(len(e) if isinstance(e, bytes) else 2 * e.size for e in enc)
+        buf = bytearray(total)
+        if not total:
+            return buf
+        base = ctypes.addressof((ctypes.c_char * total).from_buffer(buf))
+        off = 0
+        for e in enc:
+            if isinstance(e, bytes):
+                buf[off:off + len(e)] = e
+                off += len(e)
+            else:
+                if e.size:
+                    W.gen_lib().dcg_hex_upper(e.ctypes.data, e.size, base + off)
+                off += 2 * e.size
+        return buf
+
+    def __str__(self) -> str:
+        return self.tobytes().decode("ascii")
 
 
 class Func:
     def __init__(self, name: str):
         self.name = name
-        self.lines: list[str] = []
+        self.lines: list = []
         self.n = 0
         self.types: dict[str, str] = {}
 
@@ -25,7 +67,8 @@ class Func:
         v = f"%{self.n}"
         self.n += 1
         key = "values" if op == "tosa.const" else "value"
-        self.lines.append(f'    {v} = "{op}"() <{{{key} = dense<{hexlit(arr)}> : {ty}}}> : () -> {ty}')
+        self.lines.append(Text([f'    {v} = "{op}"() <{{{key} = dense<"0x', arr,
+                                f'"> : {ty}}}> : () -> {ty}']))
         self.types[v] = ty
         return v
 
@@ -38,41 +81,67 @@ class Func:
         self.types[v] = out_ty
         return v
 
-    def text(self, ret: list[str]) -> str:
+    def text(self, ret: list[str]) -> Text:
         rt = ", ".join(self.types[r] for r in ret)
         fty = f"() -> {rt}" if len(ret) == 1 else f"() -> ({rt})"
-        body = "\n".join(self.lines)
-        return (f'  "func.func"() <{{function_type = {fty}, sym_name = "{self.name}"}}> ({{\n{body}\n'
-                f'    "func.return"({", ".join(ret)}) : ({rt}) -> ()\n  }}) : () -> ()')
+        parts = [f'  "func.func"() <{{function_type = {fty}, sym_name = "{self.name}"}}> ({{\n']
+        for i, line in enumerate(self.lines):
+            if i:
+                parts.append("\n")
+            parts.extend(line.parts if isinstance(line, Text) else [line])
+        parts.append(f'\n    "func.return"({", ".join(ret)}) : ({rt}) -> ()\n  }}) : () -> ()')
+        return Text(parts)
 
 
-def module(funcs: list[str]) -> str:
-    return '"builtin.module"() ({\n' + "\n".join(funcs) + "\n}) : () -> ()\n"
+def module_text(funcs: list[Text]) -> Text:
+    parts = ['"builtin.module"() ({\n']
+    for i, f in enumerate(funcs):
+        if i:
+            parts.append("\n")
+        parts.extend(f.parts)
+    parts.append("\n}) : () -> ()\n")
+    return Text(parts)
+
+
+def module(funcs: list[Text]) -> str:
+    return str(module_text(funcs))
 
 
 FM = "fastmath = #arith.fastmath<none>"
 
 
 def config1_text() -> str:
+    return str(config1_module())
+
+
+def config1_module() -> Text:
     d = W.config1()
     ty = "tensor<1024x1024xf32>"
     f = Func("main")
     a, b = f.const(d["A"], ty), f.const(d["B"], ty)
     r = f.op("arith.addf", [a, b], ty, FM)
-    return module([f.text([r])])
+    return module_text([f.text([r])])
 
 
 def config2_text(side: int = 4096) -> str:
+    return str(config2_module(side))
+
+
+def config2_module(side: int = 4096) -> Text:
     d = W.config2(side)
     ty = f"tensor<{side}x{side}xf32>"
     f = Func("main")
     env = {k: f.const(d[k], ty) for k in "ABCD"}
     for op, a, b, t in W.CHAIN2:
         env[t] = f.op("arith." + op, [env[a], env[b]], ty, FM)
-    return module([f.text([env["t6"]])])
+    return module_text([f.text([env["t6"]])])
 
 
 def config3_text(dtype: str, rows: int = 8192, cols: int = 2048) -> str:
+    return str(config3_module(dtype, rows, cols))
+
+
+def config3_module(dtype: str, rows: int = 8192, cols: int = 2048) -> Text:
     d = W.config3(dtype, rows, cols)
     ty = f"tensor<{rows}x{cols}x{dtype}>"
     f = Func("main")
@@ -83,10 +152,14 @@ def config3_text(dtype: str, rows: int = 8192, cols: int = 2048) -> str:
     outs.append(f.op("arith.shli", [X, S], ty, ov))
     outs.append(f.op("arith.divsi", [Xd, Yd], ty))
     outs.append(f.op("arith.remsi", [Xd, Yd], ty))
-    return module([f.text(outs)])
+    return module_text([f.text(outs)])
 
 
 def config4_text(n: int = 16 * 1024 * 1024, prerounded: bool = False) -> str:
+    return str(config4_module(n, prerounded))
+
+
+def config4_module(n: int = 16 * 1024 * 1024, prerounded: bool = False) -> Text:
     d = W.config4(n, prerounded)
     f32, bf, h = f"tensor<{n}xf32>", f"tensor<{n}xbf16>", f"tensor<{n}xf16>"
     i32, i1 = f"tensor<{n}xi32>", f"tensor<{n}xi1>"
@@ -103,10 +176,14 @@ def config4_text(n: int = 16 * 1024 * 1024, prerounded: bool = False) -> str:
     fp = f.op("arith.sitofp", [ints], f32)
     c1 = f.op("arith.cmpf", [x, inr], i1, "fastmath = #arith.fastmath<none>, predicate = 4 : i64")
     c2 = f.op("arith.cmpf", [x, inr], i1, "fastmath = #arith.fastmath<none>, predicate = 13 : i64")
-    return module([f.text([t1, t2, e1, e2, si, fp, c1, c2])])
+    return module_text([f.text([t1, t2, e1, e2, si, fp, c1, c2])])
 
 
 def config5_text(funcs: int = 4096, side: int = 256, weight_side: int = 16384) -> str:
+    return str(config5_module(funcs, side, weight_side))
+
+
+def config5_module(funcs: int = 4096, side: int = 256, weight_side: int = 16384) -> Text:
     ty = f"tensor<{side}x{side}xf32>"
     out = []
     for i in range(funcs):
@@ -124,7 +201,7 @@ def config5_text(funcs: int = 4096, side: int = 256, weight_side: int = 16384) -
         c = f.const(w, wt, op="tosa.const")
         r = f.op("tosa.transpose", [c], wt, "perms = array<i32: 1, 0>")
         out.append(f.text([r]))
-    return module(out)
+    return module_text(out)
 
 
 LAYERWISE = "builtin.module(func.func(tosa-layerwise-constant-fold,canonicalize))"

@@ -2,7 +2,9 @@
 
 No public dataset is involved: every tensor is generated from SplitMix64
 (the generator of mlirpass's fuzzer, fuzz/src/rng.rs:1-38, restated here)
-with the seed `config * 1000 + tensor index`.  All arrays are raw element
+with the seed `config * 1000 + tensor index`.  The *_np functions are the
+numpy definitions; libdcfgen.so (gen/dcf_gen.c) computes the same values
+fast enough for the full-size configurations.  All arrays are raw element
 storage (uint bit patterns or float32 views) as the fold library takes them.
 
   config 1  two 1024x1024 f32 uniform[-1,1), one addf
@@ -23,6 +25,8 @@ storage (uint bit patterns or float32 views) as the fold library takes them.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 GOLDEN = np.uint64(0x9E3779B97F4A7C15)
@@ -30,8 +34,9 @@ M1 = np.uint64(0xBF58476D1CE4E5B9)
 M2 = np.uint64(0x94D049BB133111EB)
 
 
-def splitmix64(seed: int, n: int, start: int = 0) -> np.ndarray:
-    """Outputs start..start+n-1 of SplitMix64 seeded with `seed`."""
+def splitmix64_np(seed: int, n: int, start: int = 0) -> np.ndarray:
+    """Outputs start+1 .. start+n of SplitMix64 seeded with `seed` (numpy:
+    the definition that libdcfgen.so restates)."""
     with np.errstate(over="ignore"):
         i = np.arange(start + 1, start + n + 1, dtype=np.uint64)
         z = np.uint64(seed) + i * GOLDEN
@@ -40,16 +45,71 @@ def splitmix64(seed: int, n: int, start: int = 0) -> np.ndarray:
         return z ^ (z >> np.uint64(31))
 
 
-def uniform_f32(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
-    u = (splitmix64(seed, n) >> np.uint64(40)).astype(np.float64) / float(1 << 24)
+def uniform_f32_np(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
+    u = (splitmix64_np(seed, n) >> np.uint64(40)).astype(np.float64) / float(1 << 24)
     return (lo + (hi - lo) * u).astype(np.float32)
+
+
+def uniform_bf16_bits_np(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
+    """bf16 bit patterns of uniform[lo, hi) values (round to nearest even)."""
+    x = uniform_f32_np(seed, n, lo, hi).view(np.uint32)
+    rounded = x + np.uint32(0x7FFF) + ((x >> np.uint32(16)) & np.uint32(1))
+    return (rounded >> np.uint32(16)).astype(np.uint16)
+
+
+_gen = None
+
+
+def gen_lib():
+    """libdcfgen.so: the same generators in C (built on first use)."""
+    global _gen
+    if _gen is None:
+        import ctypes
+        from .build import GEN_LIB, build_gen
+        if not os.path.exists(GEN_LIB):
+            build_gen()
+        L = ctypes.CDLL(GEN_LIB)
+        u64, vp, dbl = ctypes.c_uint64, ctypes.c_void_p, ctypes.c_double
+        L.dcg_splitmix64.argtypes = [u64, u64, u64, vp]
+        L.dcg_uniform_f32.argtypes = [u64, u64, dbl, dbl, vp]
+        L.dcg_uniform_bf16.argtypes = [u64, u64, dbl, dbl, vp]
+        L.dcg_hex_upper.argtypes = [vp, u64, vp]
+        for f in (L.dcg_splitmix64, L.dcg_uniform_f32, L.dcg_uniform_bf16, L.dcg_hex_upper):
+            f.restype = None
+        _gen = L
+    return _gen
+
+
+def splitmix64(seed: int, n: int, start: int = 0) -> np.ndarray:
+    """Outputs start+1 .. start+n of SplitMix64 seeded with `seed`."""
+    out = np.empty(n, dtype=np.uint64)
+    gen_lib().dcg_splitmix64(seed & 0xFFFFFFFFFFFFFFFF, start, n, out.ctypes.data)
+    return out
+
+
+def uniform_f32(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    gen_lib().dcg_uniform_f32(seed, n, lo, hi, out.ctypes.data)
+    return out
 
 
 def uniform_bf16_bits(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
     """bf16 bit patterns of uniform[lo, hi) values (round to nearest even)."""
-    x = uniform_f32(seed, n, lo, hi).view(np.uint32)
-    rounded = x + np.uint32(0x7FFF) + ((x >> np.uint32(16)) & np.uint32(1))
-    return (rounded >> np.uint32(16)).astype(np.uint16)
+    out = np.empty(n, dtype=np.uint16)
+    gen_lib().dcg_uniform_bf16(seed, n, lo, hi, out.ctypes.data)
+    return out
+
+
+def hex_upper(a: np.ndarray) -> str:
+    """Uppercase hex of an array's raw bytes (a dense<"0x…"> body)."""
+    b = np.ascontiguousarray(a).reshape(-1).view(np.uint8)
+    out = bytearray(2 * b.size)
+    if b.size:
+        import ctypes
+        buf = (ctypes.c_char * len(out)).from_buffer(out)
+        gen_lib().dcg_hex_upper(b.ctypes.data, b.size, ctypes.addressof(buf))
+        del buf
+    return out.decode("ascii")
 
 
 def normal_f32(seed: int, n: int, sigma: float) -> np.ndarray:

@@ -415,3 +415,34 @@ def test_canonicalize_by_element_ranges_prints_the_same(gpus, ranges, monkeypatc
     f = parse_funcs(out)["main"]
     d = [f.defs.get(v) for v in f.ret.operands]
     assert d[1].const.splat and d[5].name == "arith.divsi"
+
+
+def test_engines_sharing_a_gpu_batch_small_folds_safely(monkeypatch, oracle):
+    # Ten independent addf folds of 2^18-element constants: split into three
+    # element ranges on one GPU, each of the three engines has ten small
+    # folds of one kind in the same round and sends them through the
+    # library's allocation-free batch entry point from its own thread at the
+    # same time.  The printed module must equal the one-engine module, and
+    # every folded constant the oracle's sum.
+    n, k = 1 << 18, 10
+    F = f"tensor<{n}xf32>"
+    fm = "<{fastmath = #arith.fastmath<none>}>"
+    rng = np.random.default_rng(11)
+    vals = [rng.standard_normal(n).astype(np.float32) for _ in range(2 * k)]
+    lines = [f'    %c{i} = "arith.constant"() <{{value = dense<"0x{_hex(v.view(np.uint32))}"> : {F}}}> : () -> {F}'
+             for i, v in enumerate(vals)]
+    lines += [f'    %{i} = "arith.addf"(%c{2 * i}, %c{2 * i + 1}) {fm} : ({F}, {F}) -> {F}' for i in range(k)]
+    tys = ", ".join([F] * k)
+    text = ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({tys}), sym_name = "main"}}> ({{\n'
+            + "\n".join(lines) + f'\n    "func.return"({", ".join(f"%{i}" for i in range(k))}) : ({tys}) -> ()\n'
+            '  }) : () -> ()\n}) : () -> ()\n')
+    one, s1 = opt.run(text, "canonicalize", n_gpus=1)
+    monkeypatch.setenv("DCF_OPT_RANGES_PER_GPU", "3")
+    for _ in range(3):
+        many, sn = opt.run(text, "canonicalize", n_gpus=1)
+        assert many == one
+        assert sn["folds"] == s1["folds"] == k
+    for i, d in enumerate(consts_returned(one)):
+        want = oracle.binary("addf", "f32", vals[2 * i], vals[2 * i + 1]).out
+        assert np.array_equal(full(d, n), want.astype(np.uint64)), i
