@@ -51,6 +51,12 @@ typedef struct dcf_opt_stats {
 #define DCF_OPT_SPLIT_INPUT_FILE 1
 #define DCF_OPT_LOCAL_SCOPE 2
 #define DCF_OPT_DEBUGINFO 4
+/* Print every parsed constant of up to 100 elements (other than i1) through
+ * the element printer (dcf_opt_print_element) instead of as its input text,
+ * as the reference re-reads every dense attribute at import
+ * (src/ir.rs:2149-2164).  Without it such constants keep their input text,
+ * which is already in this form when mlir-opt printed the input. */
+#define DCF_OPT_REFORMAT 8
 
 int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int flags,
                 char** out, size_t* out_len, dcf_opt_stats* stats);
@@ -60,6 +66,20 @@ int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, 
 void dcf_opt_free(char* p);
 
 const char* dcf_opt_last_error(void);
+
+/* The text of one element of a dense attribute whose element type is
+ * `dtype` (a dcf_dtype of dcfold.h), as the printer writes it and as
+ * mlir-opt does: a float in six-digit scientific form ("1.000000e+00") when
+ * that text parses back to the same bits, else in the shortest form that
+ * round-trips ("2.00000024", "3.0757404601899907E-5") when it has a decimal
+ * point, else as its hex bit pattern ("0x7FC00000"); an integer in decimal,
+ * i1 as true / false.  This decides the printed text of every folded
+ * constant of up to 100 elements, which mlirpass must print byte for byte
+ * as mlir-opt does (its printing goes through mlirformat's Const ->
+ * Attribute, src/ir.rs:2149-2164).  Writes the text and a NUL into out
+ * (cap bytes); returns its length, or a negative value if dtype is not an
+ * element type or cap is too small. */
+int dcf_opt_print_element(int dtype, unsigned long long bits, char* out, size_t cap);
 
 #ifdef __cplusplus
 }

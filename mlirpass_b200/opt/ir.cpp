@@ -307,23 +307,16 @@ bool parse_float_literal(const std::string& tok, int dtype, uint64_t* bits) {
   return end && *end == 0;
 }
 
-// MLIR prints a float in "%.6e" form when that form parses back to the same
-// bits, and otherwise in a form that keeps every bit; the hex bit pattern
-// (which MLIR also accepts) stands in for that second form here.
+// A float element as mlir-opt prints it (float_text.cpp): six-digit
+// scientific form when that parses back to the same bits, else the
+// shortest round-trip decimal form, else the hex bit pattern.
 std::string print_float_literal(uint64_t bits, int dtype) {
   Layout L;
   if (!layout_of(dtype, &L)) return "0";
-  const double v = (dtype == DCF_F64) ? [&] { double d; memcpy(&d, &bits, 8); return d; }()
-                                       : widen_to_double(bits, L);
-  if (std::isfinite(v)) {
-    char buf[64];
-    snprintf(buf, sizeof buf, "%.6e", v);
-    uint64_t back = 0;
-    if (parse_float_literal(buf, dtype, &back) && back == bits) return buf;
-  }
-  char buf[40];
-  snprintf(buf, sizeof buf, "0x%0*llX", (int)(2 * elem_bytes(dtype)), (unsigned long long)bits);
-  return buf;
+  auto back = [](const std::string& text, uint64_t* out, void* ctx) {
+    return parse_float_literal(text, *(const int*)ctx, out);
+  };
+  return mlir_float_text(bits, L.E, L.M, back, &dtype);
 }
 
 std::string print_int_literal(uint64_t bits, int dtype) {
@@ -433,7 +426,7 @@ size_t top_level_loc(const std::string& t) {
 
 class Parser {
  public:
-  Parser(std::string_view s, Module& m) : s_(s), m_(m) { find_hex_literals(); }
+  Parser(std::string_view s, Module& m, bool reformat) : s_(s), m_(m), reformat_(reformat) { find_hex_literals(); }
 
   Op* parse_top() {
     scopes_.emplace_back();
@@ -490,6 +483,9 @@ class Parser {
   const std::string_view s_;
   std::string sub(size_t a, size_t n = std::string_view::npos) const { return std::string(s_.substr(a, n)); }
   Module& m_;
+  // Print parsed constants of up to 100 elements through the element
+  // printer instead of as their input text.
+  const bool reformat_;
   size_t p_ = 0;
   struct Scope {
     std::unordered_map<std::string, std::vector<Value*>> names;
@@ -992,15 +988,15 @@ class Parser {
       memcpy(d->host.data(), &bits, d->es);
     }
     op->cst = d;
-    op->cst_text = true;
+    op->cst_text = !(reformat_ && d->n <= 100 && d->dtype != DCF_I1);
   }
 };
 
 }  // namespace
 
-std::unique_ptr<Module> parse_module(std::string_view text) {
+std::unique_ptr<Module> parse_module(std::string_view text, bool reformat) {
   auto m = std::make_unique<Module>();
-  Parser p(text, *m);
+  Parser p(text, *m, reformat);
   m->top = p.parse_top();
   return m;
 }

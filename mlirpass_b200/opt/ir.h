@@ -211,7 +211,10 @@ class Module {
 
 // Parse a module in MLIR's generic form.  `text` must outlive the module
 // (hex literals are decoded from it lazily).  Throws std::runtime_error.
-std::unique_ptr<Module> parse_module(std::string_view text);
+// reformat: constants of up to 100 elements (not i1) print through the
+// element printer, as the reference re-reads every dense attribute at
+// import (src/ir.rs:2149-2164), instead of as their input text.
+std::unique_ptr<Module> parse_module(std::string_view text, bool reformat = false);
 
 // Print the module in generic form.  Device-resident constants are fetched
 // through `fetch` (which fills DenseValue::host or returns hex digits).
@@ -250,5 +253,10 @@ std::string print_module(Module& m, const PrintHooks& hooks);
 bool parse_float_literal(const std::string& tok, int dtype, uint64_t* bits);
 std::string print_float_literal(uint64_t bits, int dtype);
 std::string print_int_literal(uint64_t bits, int dtype);
+// The text of a float element (E exponent bits, M mantissa bits) as
+// mlir-opt prints it; parse_back(text, &bits, ctx) reads a candidate text
+// back into the element type.
+std::string mlir_float_text(uint64_t bits, int E, int M, bool (*parse_back)(const std::string&, uint64_t*, void*),
+                            void* ctx);
 
 }  // namespace dco

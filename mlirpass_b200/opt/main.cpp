@@ -171,7 +171,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
   std::vector<dco::PrintedModule> parts;
   for (size_t i = 0; i < chunks.size(); i++) {
     auto t0 = Clock::now();
-    mods.push_back(dco::parse_module(chunks[i]));
+    mods.push_back(dco::parse_module(chunks[i], (flags & DCF_OPT_REFORMAT) != 0));
     dco::Module& m = *mods.back();
     total.parse_ms += ms_since(t0);
     if (i == 0 && is_pinned(text))
@@ -248,6 +248,27 @@ extern "C" int dcf_opt_run(const char* text, size_t len, const char* pipeline, i
 extern "C" void dcf_opt_free(char* p) { out_free(p); }
 
 extern "C" const char* dcf_opt_last_error(void) { return g_opt_err.c_str(); }
+
+extern "C" int dcf_opt_print_element(int dtype, unsigned long long bits, char* out, size_t cap) {
+  std::string s;
+  switch (dtype) {
+    case DCF_F16: case DCF_BF16: case DCF_F32: case DCF_F64: case DCF_F8E5M2: case DCF_F8E4M3: case DCF_F8E3M4:
+      s = dco::print_float_literal(bits, dtype);
+      break;
+    case DCF_I1: case DCF_I8: case DCF_I16: case DCF_I32: case DCF_I64:
+      s = dco::print_int_literal(bits, dtype);
+      break;
+    default:
+      g_opt_err = "not an element type";
+      return -1;
+  }
+  if (!out || s.size() + 1 > cap) {
+    g_opt_err = "output buffer too small";
+    return -1;
+  }
+  memcpy(out, s.c_str(), s.size() + 1);
+  return (int)s.size();
+}
 
 #ifdef DCFOLD_OPT_MAIN
 int main(int argc, char** argv) {

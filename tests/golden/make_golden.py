@@ -2,7 +2,7 @@
 
 Run here (the container that has the reference checkout):
 
-    python tests/golden/make_golden.py [/path/to/mlirpass]
+    python tests/golden/make_golden.py /path/to/mlirpass
 
 It reads mlirpass's `tests/fixtures/<stem>.in.mlir` (the input, as
 mlir-opt 23.1.5 prints it) and `<stem>.generic.mlir` (mlir-opt's output of
@@ -10,8 +10,8 @@ the fixture's canonicalize RUN line), for every fixture whose pipeline is a
 plain canonicalize.  For each function, every value returned by `func.return`
 or stored by `memref.store` that is produced by a hot-path fold op whose
 operands are all constants becomes one case; the expected outcome is read at
-the same position of the output function: a constant (folded, with its value) or the same op
-(not folded).  Cases the output rewrote into something else are dropped.
+the same position of the output function: a constant (folded, with its value
+and the exact text mlir-opt printed for it) or the same op (not folded).  Cases the output rewrote into something else are dropped.
 
 Math dialect fixtures (ArithFolder::math, src/patterns/math/canonicalize.rs)
 contribute the exact folds.  Each case is also labelled with the shortcut,
@@ -32,8 +32,6 @@ import sys
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 from mlir_text import FLOATS, INTS, parse_funcs, parse_type  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-FIX = os.path.join(REF, "tests", "fixtures")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "fold_vectors.json")
 
 BINARY_F = {"addf", "subf", "mulf", "divf", "maximumf", "minimumf", "maxnumf", "minnumf", "remf"}
@@ -207,15 +205,18 @@ def sinks(f):
 
 
 def main():
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the mlirpass checkout>")
+    fix = os.path.join(sys.argv[1], "tests", "fixtures")
     cases = []
-    stems = sorted(f[:-5] for f in os.listdir(FIX) if f.endswith(".args"))
+    stems = sorted(f[:-5] for f in os.listdir(fix) if f.endswith(".args"))
     for stem in stems:
-        with open(os.path.join(FIX, stem + ".args")) as fh:
+        with open(os.path.join(fix, stem + ".args")) as fh:
             args = fh.read().replace("\n", " ")
         if not plain_canonicalize(args):
             continue
-        pin = os.path.join(FIX, stem + ".in.mlir")
-        pout = os.path.join(FIX, stem + ".generic.mlir")
+        pin = os.path.join(fix, stem + ".in.mlir")
+        pout = os.path.join(fix, stem + ".generic.mlir")
         if not (os.path.exists(pin) and os.path.exists(pout)):
             continue
         a_chunks = open(pin).read().split("// -----")
@@ -257,9 +258,11 @@ def main():
                     if gop is None:
                         continue
                     if gop.name in ("arith.constant", "tosa.const") and gop.const is not None:
+                        key = "value" if gop.name == "arith.constant" else "values"
                         exp = {"status": "folded", "splat": gop.const.splat,
                                "dtype": gop.const.ty.elem,
-                               "bits": [format(x, "x") for x in gop.const.bits]}
+                               "bits": [format(x, "x") for x in gop.const.bits],
+                               "text": gop.prop_map[key]}
                     elif gop.name == op.name:
                         exp = {"status": "not_folded"}
                     else:

@@ -75,9 +75,10 @@ def render(c):
             f'\n    "func.return"({ret}) : ({rty}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
 
 
-@pytest.mark.parametrize("case", CASES, ids=[case_id(c) for c in CASES])
-def test_golden_through_canonicalize(case):
-    out, _ = opt.run(render(case), "canonicalize")
+def check_golden_output(case, out):
+    """The returned value is the fixture's: the op left in place, or a
+    constant with the fixture's bits whose attribute text is exactly the
+    text mlir-opt printed for it."""
     f = parse_funcs(out)["t"]
     d = f.defs.get(f.ret.operands[0])
     exp = case["expected"]
@@ -91,6 +92,14 @@ def test_golden_through_canonicalize(case):
         assert set(got) == {want[0]}, (got, want)
     else:
         assert got == want, (got, want)
+    key = "value" if d.name == "arith.constant" else "values"
+    assert d.prop_map[key] == exp["text"], (d.prop_map[key], exp["text"])
+
+
+@pytest.mark.parametrize("case", CASES, ids=[case_id(c) for c in CASES])
+def test_golden_through_canonicalize(case):
+    out, _ = opt.run(render(case), "canonicalize")
+    check_golden_output(case, out)
 
 
 def consts_returned(out, name="main"):
