@@ -1,26 +1,42 @@
-"""Benchmark: dense-constant fold GB/s (in+out) on B200.
+"""Benchmark: dense-constant fold GB/s (in+out) and pass wall time on B200.
 
-Workload (one step): the 4096x4096 f32 fold chain — four dense constants
-A, B, C, D (uniform[-4,4), 0.5% exact zeros in the divisor) folded through
-addf, mulf, subf, divf, maximumf, minimumf: six elementwise folds of
-16,777,216 elements, 192 MiB of algorithmic traffic each (two 64 MiB
-operands in, one 64 MiB result out), 1.125 GiB per step.
+Workload (one step): configuration 2, the 4096x4096 f32 fold chain — four
+dense constants A, B, C, D (uniform[-4,4), 0.5% exact zeros in the divisor)
+folded through addf, mulf, subf, divf, maximumf, minimumf: six elementwise
+folds of 16,777,216 elements, 192 MiB of algorithmic traffic each (two
+64 MiB operands in, one 64 MiB result out), 1.125 GiB per step.
 
-  value  GB/s of algorithmic bytes with the constants resident in HBM:
-         the six fold kernels launched through the device entry points,
-         each timed with CUDA events on its launch stream; a 256 MiB
-         read-only pass evicts L2 before every fold so each reads HBM and
-         no dirty lines are written back inside the timed kernel;
-  e2e    the same bytes through the host C ABI (dcf_binary) from pinned
-         host buffers: every fold copies its two operands host->device and
-         its result device->host inside the timed region;
+  value  GB/s of algorithmic bytes with the constants resident in HBM: the
+         six fold kernels back to back through the device entry points,
+         timed per step with CUDA events on the launch stream (each fold
+         pays the write-back of the previous one); a 256 MiB write evicts
+         L2 between steps;
+  roofline  each fold kernel alone (a 256 MiB read evicts L2 before it),
+         achieved = bytes per launch / mean launch time, against the
+         measured HBM copy bandwidth;
+  e2e    the same configuration end to end through the pass driver's C ABI
+         (dcf_opt_run): its MLIR text (537 MB of dense<"0x..."> literals)
+         in pageable host memory, `canonicalize`, the run phase timed as
+         the reference's bench does (fuzz/src/bench.rs:55-66): every fold,
+         with the literals' copies to the GPU and every folded constant
+         back in host memory; GB/s = the six folds' algorithmic bytes per
+         run.  Every printed module is checked against the expected results
+         (tests/golden/config_digests.json) before the line is printed;
+  pass_config5  configuration 5 (4096 functions + the 16384^2 bf16
+         transpose, 5.4 GB of text) through
+         builtin.module(func.func(tosa-layerwise-constant-fold,canonicalize)),
+         same timing and check;
   cpu_baseline  the oracle (the scalar C restatement of the reference's
          fold loop, which runs single-threaded in the reference) timed on
          this host on a bounded sample.
 
-Multi-GPU: one process per GPU (torchrun); each rank folds its own copy of
-the chain — one isolated function per GPU, no data-path collective — and
-`value` is the total bytes over the slowest rank's time (weak scaling).
+Multi-GPU (strong scaling: one module, fixed total work): one process per
+GPU (torchrun).  For `value` each rank folds one contiguous element range
+of every constant — the split the pass driver makes for a bare
+canonicalize — with no data-path collective; value = the step's bytes over
+the slowest rank's time.  For `e2e` and `pass_config5` rank 0 runs the
+module through the pass driver on all N GPUs while the other ranks wait on
+the host.
 
 `--impl reference` times the reference's CPU fold path instead: the oracle
 port with all host threads (the reference cannot be built here: no Rust
@@ -48,6 +64,9 @@ FOLD_BYTES = 3 * 4 * N                 # two f32 operands in, one f32 result out
 CHAIN = [("addf", "A", "B", "t1"), ("mulf", "t1", "C", "t2"), ("subf", "t2", "D", "t3"),
          ("divf", "t3", "D", "t4"), ("maximumf", "t4", "A", "t5"), ("minimumf", "t5", "B", "t6")]
 STEP_BYTES = FOLD_BYTES * len(CHAIN)
+# config 5: 4096 functions x (addf 12 + mulf 12 + reciprocal 8 bytes per
+# element of 65,536 f32) + the 16384^2 bf16 transpose (4 bytes per element)
+CONFIG5_BYTES = 4096 * 65536 * (12 + 12 + 8) + 16384 * 16384 * 4
 METRIC = "dense-constant fold GB/s (in+out)"
 CONFIG = {
     "workload": "4x 4096x4096 f32 dense constants folded by the chain addf, mulf, subf, divf, maximumf, "
@@ -176,9 +195,87 @@ def barrier(world):
 
 # ---------------------------------------------------------------- our arm
 
+def row_block(world: int, rank: int) -> tuple[int, int]:
+    """This rank's element range of each constant: the module's folds split
+    into one contiguous range per GPU (boundaries on multiples of 4096
+    elements), as the pass driver splits a bare canonicalize's constants."""
+    lo = (N * rank // world) // 4096 * 4096
+    hi = N if rank == world - 1 else (N * (rank + 1) // world) // 4096 * 4096
+    return lo, hi
+
+
+def wait_for_rank0(world: int, rank: int, key: str):
+    """Ranks other than 0 wait, on the host, while rank 0 drives every GPU
+    through the pass driver (no kernel of theirs runs meanwhile)."""
+    if world == 1:
+        return
+    import datetime
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
+    if rank == 0:
+        store.set(key, "1")
+    else:
+        store.wait([key], datetime.timedelta(seconds=900))
+
+
+def digests():
+    with open(os.path.join(ROOT, "tests", "golden", "config_digests.json")) as fh:
+        return json.load(fh)
+
+
+def verify_module(out, config: str) -> bool:
+    """Check a printed module's returned values against the committed
+    digests of the configuration's expected results (computed from the
+    oracle by tests/golden/make_config_digests.py); a mismatch ends the run
+    without a bench line."""
+    for d in (os.path.join(ROOT, "tests"), os.path.join(ROOT, "tests", "golden")):
+        if d not in sys.path:
+            sys.path.insert(0, d)
+    from full_module import returns_digest, scan
+    got = returns_digest(scan(bytes(out)))
+    if got != digests()[config]:
+        raise SystemExit(f"{config}: the printed module differs from the expected results ({got})")
+    return True
+
+
+def pass_runs(opt, text, pipeline, n_gpus, warmup, steps, config):
+    """Run a pipeline over pageable module text `warmup + steps` times; the
+    run phases of the last `steps` are kept; the last output is checked."""
+    runs, out = [], None
+    for r in range(warmup + steps):
+        t0 = time.perf_counter()
+        out, st = opt.run(text, pipeline, n_gpus=n_gpus, as_array=True)
+        st["wall_ms"] = (time.perf_counter() - t0) * 1e3
+        if r >= warmup:
+            runs.append(st)
+        if r + 1 < warmup + steps:
+            del out
+    ok = verify_module(out, config)
+    del out
+    return runs, ok
+
+
+def pass_summary(runs, algo_bytes, config, pipeline, text_bytes, n_gpus, ok):
+    mean = lambda k: statistics.mean(s[k] for s in runs)
+    run_ms = mean("run_ms")
+    return {"config": config, "pipeline": pipeline, "n_gpus": n_gpus, "text_bytes": text_bytes,
+            "text_memory": "pageable", "runs": len(runs),
+            "run_ms": round(run_ms, 3), "run_ms_best": round(min(s["run_ms"] for s in runs), 3),
+            "call_ms": round(mean("call_ms"), 2), "parse_ms": round(mean("parse_ms"), 2),
+            "print_ms": round(mean("print_ms"), 2), "upload_ms": round(mean("upload_ms"), 2),
+            "fold_ms": round(mean("fold_ms"), 2), "download_ms": round(mean("download_ms"), 2),
+            "folds": runs[-1]["folds"], "refused": runs[-1]["refused"],
+            "h2d_bytes": runs[-1]["h2d_bytes"], "d2h_bytes": runs[-1]["d2h_bytes"],
+            "algorithmic_bytes": algo_bytes,
+            "GB/s": round(algo_bytes / (run_ms * 1e-3) / 1e9, 2) if algo_bytes else None,
+            "verified": ok}
+
+
 def run_gpu(args):
     import torch
     import mlirpass_b200 as dcf
+    from mlirpass_b200 import mlir_gen as G
+    from mlirpass_b200 import opt
     from mlirpass_b200 import workloads as W
 
     world, rank, local = dist_setup(args.gpus)
@@ -188,89 +285,123 @@ def run_gpu(args):
     dev = torch.device("cuda", local)
 
     d = W.config2(SIDE)
+    lo, hi = row_block(world, rank)
+    n = hi - lo
+    fold_bytes = 3 * 4 * n
     host = {k: d[k] for k in "ABCD"}
-    # device-resident operands and results
-    res = {k: torch.from_numpy(host[k]).to(dev) for k in "ABCD"}
+    # device-resident operands (this rank's rows) and results
+    res = {k: torch.from_numpy(host[k][lo:hi].copy()).to(dev) for k in "ABCD"}
     for _, _, _, t in CHAIN:
-        res[t] = torch.empty(N, dtype=torch.float32, device=dev)
+        res[t] = torch.empty(n, dtype=torch.float32, device=dev)
     status = torch.empty(len(CHAIN) * 2, dtype=torch.int64, device=dev)
-    flush = torch.ones(32 << 20, dtype=torch.int64, device=dev)   # 256 MiB, written once
+    flush = torch.ones(32 << 20, dtype=torch.int64, device=dev)   # 256 MiB (L2 is 126 MB)
     stream = torch.cuda.current_stream(dev)
 
-    def device_step(events=None):
+    def chain(fold_events=None, read_flush=False):
         for i, (op, a, b, t) in enumerate(CHAIN):
             st = status[2 * i:2 * i + 2]
-            flush.sum()
+            if read_flush:
+                flush.sum()
             dcf.status_reset(st, stream)
-            if events is not None:
-                events[i][0].record(stream)
-            dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=N, stream=stream)
-            if events is not None:
-                events[i][1].record(stream)
+            if fold_events is not None:
+                fold_events[i][0].record(stream)
+            dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=n, stream=stream)
+            if fold_events is not None:
+                fold_events[i][1].record(stream)
 
     for _ in range(args.warmup):
-        device_step()
+        chain(read_flush=True)
     torch.cuda.synchronize()
-    # correctness of the timed path: every fold folds, results not splat
     for i in range(len(CHAIN)):
         r = dcf.status_read(status[2 * i:2 * i + 2], stream)
         if not r.folded:
             raise SystemExit(f"fold {CHAIN[i][0]} refused at {r.first_fail_index}")
 
     clocks = Clocks(local)
+    clocks.start()
     launches0 = dcf.kernel_launches()
+    # ---- value: whole steps (the six folds back to back, each paying the
+    # write-back of the one before); between steps a 256 MiB write evicts L2.
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in CHAIN] for _ in range(args.steps)]
+    step_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     for s in range(args.steps):
-        device_step(evs[s])
+        flush.add_(1)
+        step_ev[s][0].record(stream)
+        chain()
+        step_ev[s][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    step_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in step_ev)
+    # ---- roofline: each fold alone, a 256 MiB read evicting L2 before it
+    fold_ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in CHAIN] for _ in range(args.steps)]
+    for s in range(args.steps):
+        chain(fold_ev[s], read_flush=True)
     torch.cuda.synchronize()
     barrier(world)
     value_launches = dcf.kernel_launches() - launches0
-    fold_ms = [[evs[s][i][0].elapsed_time(evs[s][i][1]) for i in range(len(CHAIN))] for s in range(args.steps)]
-    step_ms = sum(sum(x) for x in fold_ms) / args.steps
+    fold_ms = [[fold_ev[s][i][0].elapsed_time(fold_ev[s][i][1]) for i in range(len(CHAIN))]
+               for s in range(args.steps)]
     kernel_ms = sum(sum(x) for x in fold_ms) / (args.steps * len(CHAIN))
     per_fold_us = {CHAIN[i][0]: round(1000.0 * sum(fold_ms[s][i] for s in range(args.steps)) / args.steps, 2)
                    for i in range(len(CHAIN))}
+    step_ms_max = allreduce_max(step_ms, world)
+    kernel_ms_max = allreduce_max(kernel_ms, world)
 
-    # ---- e2e through the host C ABI, pinned host buffers
-    pin = {k: torch.from_numpy(host[k]).pin_memory() for k in "ABCD"}
+    # ---- e2e: the whole configuration through the pass driver, from its MLIR
+    # text in pageable host memory; rank 0 drives all `world` GPUs (the
+    # module's constants split into one element range per GPU) while the
+    # other ranks wait on the host.
+    e2e = p5 = None
+    launches1 = dcf.kernel_launches()
+    if rank == 0:
+        text2 = G.config2_module().tobytes()
+        runs2, ok2 = pass_runs(opt, text2, "canonicalize", world, args.warmup, args.steps, "config2")
+        e2e = pass_summary(runs2, STEP_BYTES, "config2", "canonicalize", len(text2), world, ok2)
+        del text2
+        if not args.no_config5:
+            text5 = G.config5_module(4096).tobytes()
+            runs5, ok5 = pass_runs(opt, text5, G.LAYERWISE, world, 1, max(1, min(args.steps, 3)), "config5")
+            p5 = pass_summary(runs5, CONFIG5_BYTES, "config5", G.LAYERWISE, len(text5), world, ok5)
+            del text5
+    pass_launches = dcf.kernel_launches() - launches1
+    wait_for_rank0(world, rank, "pass_done")
+    barrier(world)
+    clk = clocks.stop()
+
+    # ---- the host C ABI on raw operands (pinned host buffers): each fold
+    # copies its operands in and its result out
+    pin = {k: torch.from_numpy(host[k][lo:hi].copy()).pin_memory() for k in "ABCD"}
     for _, _, _, t in CHAIN:
-        pin[t] = torch.empty(N, dtype=torch.float32).pin_memory()
+        pin[t] = torch.empty(n, dtype=torch.float32).pin_memory()
     npv = {k: v.numpy() for k, v in pin.items()}
 
     def host_step():
         for op, a, b, t in CHAIN:
             f = dcf.binary(op, "f32", npv[a], npv[b], out=npv[t].view(np.uint32))
             if not f.folded:
-                raise SystemExit(f"e2e fold {op} refused")
+                raise SystemExit(f"host fold {op} refused")
 
     for _ in range(max(1, args.warmup)):
         host_step()
-    launches1 = dcf.kernel_launches()
+    launches2 = dcf.kernel_launches()
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         host_step()
-    e2e_s = time.perf_counter() - t0
+    cabi_s = time.perf_counter() - t0
     barrier(world)
-    e2e_launches = dcf.kernel_launches() - launches1
-    clk = clocks.stop()
-
-    # bit-exact agreement of the two paths
+    cabi_launches = dcf.kernel_launches() - launches2
     same = all(torch.equal(res[t].cpu(), pin[t]) for _, _, _, t in CHAIN)
-
-    step_ms_max = allreduce_max(step_ms, world)
-    kernel_ms_max = allreduce_max(kernel_ms, world)
-    e2e_ms_max = allreduce_max(e2e_s * 1000.0 / args.steps, world)
+    cabi_ms_max = allreduce_max(cabi_s * 1000.0 / args.steps, world)
+    launches = allreduce_max(float(value_launches + cabi_launches), world) + pass_launches
 
     if rank != 0:
         return
     peak, peak_kind = load_peaks()
-    gbs = world * STEP_BYTES / (step_ms_max * 1e-3) / 1e9
-    achieved = FOLD_BYTES / (kernel_ms_max * 1e-3) / 1e9
-    e2e_gbs = world * STEP_BYTES / (e2e_ms_max * 1e-3) / 1e9
+    gbs = STEP_BYTES / (step_ms_max * 1e-3) / 1e9
+    achieved = fold_bytes / (kernel_ms_max * 1e-3) / 1e9
+    traffic = load_traffic() if world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(gbs, 2),
@@ -280,26 +411,44 @@ def run_gpu(args):
         "warmup": args.warmup,
         "ms_per_step": round(step_ms_max, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (SplitMix64-seeded dense constants; no dataset)",
-        "config": dict(CONFIG, parallelism=f"{world} independent functions, one per GPU",
-                       results_bit_identical_device_vs_host_path=same),
-        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms_max, 3),
-                "h2d_bytes_per_step": 2 * 4 * N * len(CHAIN), "d2h_bytes_per_step": 4 * N * len(CHAIN),
-                "path": "dcf_binary (host C ABI), pinned host buffers, 6 calls per step"},
+        "config": dict(CONFIG, parallelism=f"one module over {world} GPU(s): each constant split into "
+                                            f"{world} element range(s), one per GPU",
+                       elements_per_gpu=n, results_bit_identical_device_vs_host_path=same),
+        "e2e": {"value": e2e["GB/s"], "unit": "GB/s", "ms_per_step": e2e["run_ms"],
+                "h2d_bytes_per_step": e2e["h2d_bytes"], "d2h_bytes_per_step": e2e["d2h_bytes"],
+                "path": "dcf_opt_run (the pass driver's C ABI) on the configuration's MLIR text in pageable "
+                        "host memory, canonicalize: the run phase (every fold, with the literals' host->device "
+                        "copies and decode and every folded constant back in host memory), as the "
+                        "reference's bench times it; the printed module is checked against the expected "
+                        "results every run",
+                "pass": e2e,
+                "c_abi_pinned": {"value": round(STEP_BYTES / (cabi_ms_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                 "ms_per_step": round(cabi_ms_max, 3),
+                                 "path": "dcf_binary (host C ABI) on raw operands in pinned host buffers, this "
+                                         "rank's rows, 6 calls per step"}},
+        "pass_config5": p5,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "ew_tma_kernel<FArith/FMinMax f32>: cp.async.bulk 16 KB tiles, 2 stages, "
                                "3 CTAs/SM; fused fold + refusal + splat test",
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
-                     "kernel_ms": round(kernel_ms_max, 5), "per_fold_us": per_fold_us},
-        "gpu_launches": int(value_launches + e2e_launches),
-        "gpu_launches_detail": {"value_path": int(value_launches), "e2e_path": int(e2e_launches)},
+                     "timing": "each fold alone, a 256 MiB read evicting L2 before it (part of its result is "
+                               "still in L2 when it ends); value times the six folds back to back",
+                     "value_frac": round(gbs / world / peak, 4),
+                     "kernel_ms": round(kernel_ms_max, 5), "per_fold_us": per_fold_us,
+                     "bytes_per_launch": fold_bytes},
+        "gpu_launches": int(launches),
+        "gpu_launches_detail": {"value_and_roofline": int(value_launches), "pass_runs": int(pass_launches),
+                                "c_abi": int(cabi_launches)},
         "clocks": clk,
     }
+    if traffic:
+        line["roofline"]["dram_rate_GBs"] = round(traffic / (kernel_ms_max * 1e-3) / 1e9, 1)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(host, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -550,40 +699,50 @@ def run_profile_kernels(args):
 
 def run_pass(args):
     """A whole pipeline through the pass driver on MLIR text: parse / run /
-    print phases, like the reference's own bench (fuzz/src/bench.rs:55-66)."""
+    print phases, like the reference's own bench (fuzz/src/bench.rs:55-66);
+    the printed module of the last run is checked against the expected
+    results before the line is printed."""
     from mlirpass_b200 import mlir_gen as G
     from mlirpass_b200 import opt
     cfg = args.workload.split(":", 1)[1]
     if cfg == "config1":
-        text, pipe = G.config1_text(), "canonicalize"
+        mod, pipe = G.config1_module(), "canonicalize"
     elif cfg == "config2":
-        text, pipe = G.config2_text(), "canonicalize"
+        mod, pipe = G.config2_module(), "canonicalize"
     elif cfg.startswith("config3"):
-        text, pipe = G.config3_text(cfg.split("-")[1] if "-" in cfg else "i32"), "canonicalize"
+        cfg = cfg if "-" in cfg else "config3-i32"
+        mod, pipe = G.config3_module(cfg.split("-")[1]), "canonicalize"
     elif cfg == "config4":
-        text, pipe = G.config4_text(), "canonicalize"
+        mod, pipe = G.config4_module(), "canonicalize"
     elif cfg == "config4b":
-        text, pipe = G.config4_text(prerounded=True), "canonicalize"
+        mod, pipe = G.config4_module(prerounded=True), "canonicalize"
     elif cfg == "config5":
-        text, pipe = G.config5_text(args.funcs), G.LAYERWISE
+        mod, pipe = G.config5_module(args.funcs), G.LAYERWISE
     else:
         raise SystemExit(f"unknown workload {args.workload}")
+    text = mod.tobytes()
     # The module text is read from page-locked host memory (the driver then
     # copies constants straight from it), unless --pageable.
     src = text if args.pageable else opt.pinned_text(text)
+    check = cfg if (cfg != "config5" or args.funcs == 4096) else None
     for n_gpus in ([int(x) for x in args.sweep_gpus.split(",")] if args.sweep_gpus else [args.gpus]):
-        _pass_line(args, opt, cfg, pipe, text, src, n_gpus)
+        _pass_line(args, opt, cfg, pipe, text, src, n_gpus, check)
 
 
-def _pass_line(args, opt, cfg, pipe, text, src, n_gpus):
+def _pass_line(args, opt, cfg, pipe, text, src, n_gpus, check):
     runs = []
-    for r in range(max(1, args.warmup) + args.steps):
+    out = None
+    total = max(1, args.warmup) + args.steps
+    for r in range(total):
         t0 = time.perf_counter()
         out, st = opt.run(src, pipe, n_gpus=n_gpus, as_array=True)
         st["wall_ms"] = (time.perf_counter() - t0) * 1e3
-        del out
         if r >= max(1, args.warmup):
             runs.append(st)
+        if r + 1 < total:
+            del out
+    verified = verify_module(out, check) if check else None
+    del out
     best = min(runs, key=lambda s: s["run_ms"])
     line = {"workload": f"pass {cfg}", "pipeline": pipe, "n_gpus": n_gpus, "text_bytes": len(text),
             "text_memory": "pageable" if args.pageable else "pinned",
@@ -595,7 +754,7 @@ def _pass_line(args, opt, cfg, pipe, text, src, n_gpus):
             "download_ms": round(best["download_ms"], 2),
             "folds": best["folds"], "refused": best["refused"],
             "h2d_bytes": best["h2d_bytes"], "d2h_bytes": best["d2h_bytes"], "batches": best["batches"],
-            "runs": len(runs)}
+            "runs": len(runs), "verified": verified}
     print(json.dumps(line), flush=True)
 
 
@@ -607,6 +766,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config 5 pass runs of the default line")
     ap.add_argument("--workload", default="chain4096",
                     help="chain4096 (the headline line), kernels, profile-kernels, or "
                          "pass:<config1|config2|config3-i8|...|config5>")

@@ -10,6 +10,7 @@ when a test asks for them.
 from __future__ import annotations
 
 import binascii
+import hashlib
 import re
 from dataclasses import dataclass
 
@@ -71,3 +72,35 @@ def scan(text) -> Module:
         pos = b + 1
     skeleton = b"".join(pieces).decode()
     return Module(text, spans, parse_funcs(skeleton))
+
+
+def entry_const(hex_upper: bytes) -> str:
+    return "const " + hashlib.sha256(hex_upper).hexdigest()
+
+
+def entry_op(name: str) -> str:
+    return "op " + name
+
+
+def combine(entries) -> str:
+    """One digest of a module's returned values: for each function in
+    order, for each returned value, `const <sha256 of its hex body>` or
+    `op <name>` (a value left unfolded)."""
+    h = hashlib.sha256()
+    for e in entries:
+        h.update(e.encode() + b"\n")
+    return h.hexdigest()
+
+
+def returns_digest(m: Module) -> str:
+    entries = []
+    for name, f in m.funcs.items():
+        for v in f.ret.operands:
+            d = f.defs.get(v)
+            k = m.literal_index(d) if d is not None else None
+            if d is not None and d.name in ("arith.constant", "tosa.const") and k is not None:
+                a, b = m.spans[k]
+                entries.append(f"{name} " + entry_const(m.text[a:b]))
+            else:
+                entries.append(f"{name} " + entry_op(d.name if d is not None else "?"))
+    return combine(entries)

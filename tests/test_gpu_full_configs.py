@@ -16,10 +16,13 @@ and packed uploads of hundreds of MB, several fold rounds, batches of 1024
 small folds through the allocation-free batch entry point, and 2^28-element
 transposes.
 """
+import json
+import os
+
 import numpy as np
 import pytest
 
-from full_module import scan
+from full_module import returns_digest, scan
 from mlirpass_b200 import mlir_gen, opt
 from mlirpass_b200 import workloads as W
 
@@ -39,6 +42,16 @@ def names(f):
     return [o.name for o in f.ops]
 
 
+DIGESTS = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "config_digests.json")))
+
+
+def same_digest(m, config):
+    """The committed digest of the configuration's results (which bench.py
+    checks every timed run against) is the digest of this output, which the
+    test has just compared value by value with the oracle."""
+    assert returns_digest(m) == DIGESTS[config], config
+
+
 def test_config1_full(oracle):
     m, st = run(mlir_gen.config1_module(), "canonicalize")
     c = W.config1()
@@ -47,6 +60,7 @@ def test_config1_full(oracle):
     want = oracle.binary("addf", "f32", c["A"], c["B"]).out
     assert np.array_equal(m.values(d, U32), want)
     assert st["folds"] == 1
+    same_digest(m, "config1")
 
 
 def test_config2_full(oracle):
@@ -60,6 +74,7 @@ def test_config2_full(oracle):
     assert names(m.funcs["main"]) == ["arith.constant", "func.return"]
     assert np.array_equal(m.values(d, U32), env["t6"])
     assert st["folds"] == 6 and st["refused"] == 0
+    same_digest(m, "config2")
 
 
 @pytest.mark.parametrize("dt", ["i8", "i32", "i64"])
@@ -84,6 +99,7 @@ def test_config3_full(dt, oracle):
     assert sorted(set(names(f))) == ["arith.constant", "arith.divsi", "func.return"]
     assert names(f).count("arith.constant") == 9          # 7 folded results + the divsi's two operands
     assert st["folds"] == 7
+    same_digest(m, f"config3-{dt}")
 
 
 def test_config4_full(oracle):
@@ -103,6 +119,7 @@ def test_config4_full(oracle):
     assert np.array_equal(m.values(si, U32), oracle.convert("fptosi", "f32", "i32", c["inrange"]).out)
     assert np.array_equal(m.values(fp, U32), oracle.convert("sitofp", "i32", "f32", c["ints"]).out)
     assert st["folds"] == 2
+    same_digest(m, "config4")
 
 
 def test_config4b_full(oracle):
@@ -119,6 +136,7 @@ def test_config4b_full(oracle):
     assert np.array_equal(m.values(si, U32), oracle.convert("fptosi", "f32", "i32", c["inrange"]).out)
     assert np.array_equal(m.values(fp, U32), oracle.convert("sitofp", "i32", "f32", c["ints"]).out)
     assert c1.name == "arith.cmpf" and c2.name == "arith.cmpf"
+    same_digest(m, "config4b")
 
 
 def test_config5_full(oracle):
@@ -139,3 +157,4 @@ def test_config5_full(oracle):
     got = m.values(f.defs[f.ret.operands[0]], U16).reshape(ws, ws)
     assert np.array_equal(got, w.T)
     assert st["folds"] == 3 * funcs + 1 and st["refused"] == 0
+    same_digest(m, "config5")

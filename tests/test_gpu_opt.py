@@ -455,3 +455,54 @@ def test_engines_sharing_a_gpu_batch_small_folds_safely(monkeypatch, oracle):
     for i, d in enumerate(consts_returned(one)):
         want = oracle.binary("addf", "f32", vals[2 * i], vals[2 * i + 1]).out
         assert np.array_equal(full(d, n), want.astype(np.uint64)), i
+
+
+def _resource_module():
+    # Constants whose values are dense_resource blobs, as operands of every
+    # kind of fold the two passes run: arith binary and cast folds under
+    # canonicalize, tosa.reciprocal and tosa.transpose under the layerwise
+    # pass.  The reference reads a resource's bytes only when lowering to
+    # SPIR-V (resource_const, src/ir.rs:662-696, called only from
+    # src/patterns/arith/to_spirv.rs:215), so its folds see no constant
+    # value and nothing folds; the blobs stay as they are.
+    F4, B4 = "tensor<4xf32>", "tensor<2x2xbf16>"
+    fm = "<{fastmath = #arith.fastmath<none>}>"
+    body = ('"builtin.module"() ({\n'
+            f'  "func.func"() <{{function_type = () -> ({F4}, tensor<4xbf16>), sym_name = "arith"}}> ({{\n'
+            f'    %0 = "arith.constant"() <{{value = dense_resource<blob_a> : {F4}}}> : () -> {F4}\n'
+            f'    %1 = "arith.constant"() <{{value = dense<[1.000000e+00, 2.000000e+00, 3.000000e+00, 4.000000e+00]> : {F4}}}> : () -> {F4}\n'
+            f'    %2 = "arith.addf"(%0, %1) {fm} : ({F4}, {F4}) -> {F4}\n'
+            f'    %3 = "arith.truncf"(%0) : ({F4}) -> tensor<4xbf16>\n'
+            f'    "func.return"(%2, %3) : ({F4}, tensor<4xbf16>) -> ()\n'
+            '  }) : () -> ()\n'
+            f'  "func.func"() <{{function_type = () -> ({B4}, {B4}), sym_name = "tosa"}}> ({{\n'
+            f'    %0 = "tosa.const"() <{{values = dense_resource<blob_w> : {B4}}}> : () -> {B4}\n'
+            f'    %1 = "tosa.transpose"(%0) <{{perms = array<i32: 1, 0>}}> : ({B4}) -> {B4}\n'
+            f'    %2 = "tosa.reciprocal"(%0) : ({B4}) -> {B4}\n'
+            f'    "func.return"(%1, %2) : ({B4}, {B4}) -> ()\n'
+            '  }) : () -> ()\n'
+            '}) : () -> ()\n')
+    meta = ('\n{-#\n  dialect_resources: {\n    builtin: {\n'
+            '      blob_a: "0x040000000000803F000000400000404000008040",\n'
+            '      blob_w: "0x02000000803F0040403F8040"\n'
+            '    }\n  }\n#-}\n')
+    return body + meta
+
+
+def check_resource_operands_stay(n_gpus):
+    text = _resource_module()
+    for pipe in ("canonicalize", mlir_gen.LAYERWISE):
+        out, st = opt.run(text, pipe, n_gpus=n_gpus)
+        fs = parse_funcs(out)
+        assert [o.name for o in fs["arith"].ops] == ["arith.constant", "arith.constant", "arith.addf",
+                                                     "arith.truncf", "func.return"], (pipe, out)
+        assert [o.name for o in fs["tosa"].ops] == ["tosa.const", "tosa.transpose", "tosa.reciprocal",
+                                                    "func.return"], (pipe, out)
+        assert st["folds"] == 0
+        assert 'blob_a: "0x040000000000803F000000400000404000008040"' in out
+        assert 'blob_w: "0x02000000803F0040403F8040"' in out
+        assert out.count("dense_resource<blob_a>") == 1 and out.count("dense_resource<blob_w>") == 1
+
+
+def test_dense_resource_operands_are_not_folded():
+    check_resource_operands_stay(1)

@@ -258,3 +258,10 @@ def test_output_buffers_given_back_are_reused_safely():
         want.setdefault(text, got)
         assert got == want[text]
         assert got.endswith(b") : () -> ()\n\n")
+
+
+def test_dense_resource_operands_are_not_folded_host_only():
+    # The same module as the GPU test: no fold sees a resource's value, so
+    # the host-only driver (which refuses any element work) prints it back.
+    from test_gpu_opt import check_resource_operands_stay
+    check_resource_operands_stay(0)
