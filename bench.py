@@ -697,6 +697,88 @@ def run_profile_kernels(args):
     print(json.dumps({"workload": "profile-kernels", "launch_rounds": 2}))
 
 
+def gpu_local_cpus(dev: int) -> list[int]:
+    """Host CPUs on the GPU's NUMA node (from sysfs), or every CPU."""
+    try:
+        import torch
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id.lower()
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as fh:
+            cpus = []
+            for part in fh.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus += list(range(int(lo), int(hi or lo) + 1))
+        allowed = os.sched_getaffinity(0)
+        return [c for c in cpus if c in allowed] or sorted(allowed)
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return sorted(os.sched_getaffinity(0))
+
+
+def run_h2d(args):
+    """The box's host<->device copy ceiling: every GPU of --gpus copies
+    1 GiB blocks from page-locked host memory at once, (a) each from its
+    own buffer, allocated by a thread bound to the GPU's NUMA node, and
+    (b) all from one shared buffer; then the same device->host.  One line
+    per mode with the aggregate and each GPU's GB/s (CUDA events per copy,
+    the aggregate over the wall time of all copies)."""
+    import torch
+    n = args.gpus
+    nbytes = 1 << 30
+    reps = max(3, args.steps)
+    shared = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    own, dev_bufs = [None] * n, [None] * n
+
+    def setup(g):
+        os.sched_setaffinity(0, gpu_local_cpus(g))
+        own[g] = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        own[g].fill_(g)
+        dev_bufs[g] = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{g}")
+
+    ts = [threading.Thread(target=setup, args=(g,)) for g in range(n)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for mode in ("own", "shared"):
+        for direction in ("h2d", "d2h"):
+            per = [0.0] * n
+            barrier_ = threading.Barrier(n)
+
+            def work(g):
+                torch.cuda.set_device(g)
+                s = torch.cuda.Stream(g)
+                host = own[g] if mode == "own" else shared
+                ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(reps)]
+                with torch.cuda.stream(s):
+                    dev_bufs[g].copy_(host, non_blocking=True) if direction == "h2d" else \
+                        host.copy_(dev_bufs[g], non_blocking=True)
+                s.synchronize()
+                barrier_.wait()
+                with torch.cuda.stream(s):
+                    for r in range(reps):
+                        ev[r][0].record(s)
+                        if direction == "h2d":
+                            dev_bufs[g].copy_(host, non_blocking=True)
+                        else:
+                            host.copy_(dev_bufs[g], non_blocking=True)
+                        ev[r][1].record(s)
+                s.synchronize()
+                per[g] = nbytes * reps / (sum(e0.elapsed_time(e1) for e0, e1 in ev) * 1e-3) / 1e9
+
+            t0 = time.perf_counter()
+            ts = [threading.Thread(target=work, args=(g,)) for g in range(n)]
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            wall = time.perf_counter() - t0
+            print(json.dumps({"workload": "h2d-ceiling", "mode": mode, "direction": direction, "n_gpus": n,
+                              "bytes_per_copy": nbytes, "copies_per_gpu": reps,
+                              "aggregate_GBs_wall": round(n * nbytes * reps / wall / 1e9, 1),
+                              "per_gpu_GBs": [round(x, 1) for x in per],
+                              "numa_local_cpus": [len(gpu_local_cpus(g)) for g in range(n)] if mode == "own" else None}),
+                  flush=True)
+
+
 def run_pass(args):
     """A whole pipeline through the pass driver on MLIR text: parse / run /
     print phases, like the reference's own bench (fuzz/src/bench.rs:55-66);
@@ -768,8 +850,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config5", action="store_true", help="skip the config 5 pass runs of the default line")
     ap.add_argument("--workload", default="chain4096",
-                    help="chain4096 (the headline line), kernels, profile-kernels, or "
-                         "pass:<config1|config2|config3-i8|...|config5>")
+                    help="chain4096 (the headline line), kernels, profile-kernels, h2d (host<->device copy "
+                         "ceiling of --gpus GPUs at once), or pass:<config1|config2|config3-i8|...|config5>")
     ap.add_argument("--funcs", type=int, default=4096, help="functions of config 5")
     ap.add_argument("--pageable", action="store_true", help="pass workloads: keep the module text in pageable memory")
     ap.add_argument("--sweep-gpus", default="", help="pass workloads: GPU counts to run in turn, e.g. 1,2,4,8")
@@ -784,6 +866,9 @@ def main():
         return
     if args.workload.startswith("pass:"):
         run_pass(args)
+        return
+    if args.workload == "h2d":
+        run_h2d(args)
         return
     if args.impl == "reference":
         run_reference(args)
