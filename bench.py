@@ -298,11 +298,13 @@ def run_gpu(args):
     stream = torch.cuda.current_stream(dev)
 
     def chain(fold_events=None, read_flush=False):
+        if not read_flush:
+            status.fill_(-1)          # the six statuses at once (all bytes 0xFF)
         for i, (op, a, b, t) in enumerate(CHAIN):
             st = status[2 * i:2 * i + 2]
             if read_flush:
                 flush.sum()
-            dcf.status_reset(st, stream)
+                dcf.status_reset(st, stream)
             if fold_events is not None:
                 fold_events[i][0].record(stream)
             dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=n, stream=stream)

@@ -18,6 +18,30 @@ template <int OP, int W> constexpr bool checked_word_op() {
                                  OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI);
 }
 
+// floor(x / d) for 0 <= x < 2^16 and 1 <= d < 2^16 on the FMA and integer
+// pipes only: no division, no reciprocal unit and no int<->float conversion
+// instruction (those run on the narrow transcendental / conversion unit,
+// which limited the lane-wise 8-bit division).  The operands become floats
+// exactly by the magic-number trick (2^23 + v has v as its low mantissa
+// bits); the reciprocal starts from the exponent-negation seed of the fast
+// inverse methods (e.g. C. Lomont, "Fast Inverse Square Root", 2003, whose
+// reciprocal form is within 12.5% of 1/d) and takes STEPS Newton-Raphson
+// steps r <- r + r (1 - d r), each squaring the relative error (2 steps:
+// < 2.5e-4, enough for x < 2^8; 3 steps: < 1e-7 with f32 rounding, enough
+// for x < 2^16), so x * r rounded to an integer is floor(x / d) or one more,
+// and one integer correction makes it exact.
+template <int STEPS>
+__device__ __forceinline__ uint32_t udiv_small(uint32_t x, uint32_t d) {
+  const float xf = __int_as_float(0x4B000000u | x) - 8388608.0f;
+  const float df = __int_as_float(0x4B000000u | d) - 8388608.0f;
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(df));
+#pragma unroll
+  for (int i = 0; i < STEPS; i++) r = __fmaf_rn(r, __fmaf_rn(-df, r, 1.0f), r);
+  uint32_t q = (uint32_t)__float_as_int(__fmaf_rn(xf, r, 8388608.0f)) - 0x4B000000u;
+  if ((int32_t)(x - q * d) < 0) q--;
+  return q;
+}
+
 template <int OP, int W> struct IOp {
   using In = typename IntW<W>::T;
   using Out = typename IntW<W>::T;
@@ -28,9 +52,8 @@ template <int OP, int W> struct IOp {
   // once (the returned mask): a shift amount of the width or more, a zero
   // divisor, and the signed minimum divided by -1; a refusing lane still
   // gets some value, which is never used.  Quotients of 8- and 16-bit
-  // lanes come from one correctly rounded f32 division: for |x| < 2^24 its
-  // error is below the distance 1/|y| from x/y to the next integer, so
-  // truncating it gives the exact quotient.
+  // lanes come from udiv_small on the magnitudes (truncating division of
+  // signed lanes: the magnitude of the quotient, then its sign).
   __device__ static __forceinline__ uint32_t word_checked(uint32_t a, uint32_t b, uint32_t& o) {
     constexpr uint32_t M = (1u << W) - 1;
     uint32_t bad = 0;
@@ -55,10 +78,12 @@ template <int OP, int W> struct IOp {
       else if constexpr (OP == DCF_SHRUI) z = x >> y;
       else if constexpr (OP == DCF_SHRSI) z = (uint32_t)(sx >> y);
       else if constexpr (OP == DCF_DIVUI || OP == DCF_REMUI) {
-        const uint32_t q = (uint32_t)truncf(__fdiv_rn((float)x, (float)y));
+        const uint32_t q = udiv_small<W == 8 ? 2 : 3>(x, y);
         z = OP == DCF_DIVUI ? q : x - q * y;
       } else {
-        const int32_t q = (int32_t)truncf(__fdiv_rn((float)sx, (float)sy));
+        const uint32_t ax = (uint32_t)(sx < 0 ? -sx : sx), ay = (uint32_t)(sy < 0 ? -sy : sy);
+        const uint32_t qm = udiv_small<W == 8 ? 2 : 3>(ax, ay);
+        const int32_t q = ((sx ^ sy) < 0) ? -(int32_t)qm : (int32_t)qm;
         z = (uint32_t)(OP == DCF_DIVSI ? q : sx - q * sy);
       }
       r |= (z & M) << (W * k);

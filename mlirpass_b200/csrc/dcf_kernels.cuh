@@ -14,6 +14,7 @@
 #include <stdint.h>
 
 #include <type_traits>
+#include <utility>
 
 #include "dcf_elem.cuh"
 #include "dcf_launch.h"
@@ -58,6 +59,20 @@ __device__ __forceinline__ void report(dcf_status* st, uint64_t my_fail, bool no
   if (__any_sync(full, nonsplat)) {
     if (lane == 0) st->splat_word = 0u;
   }
+}
+
+// Programmatic dependent launch: the fold kernels are launched so that the
+// next kernel in the stream may start while this one drains (its CTAs take
+// the SM slots this grid's CTAs leave).  Each fold kernel first waits until
+// the grid before it has completed and its writes are visible
+// (griddepcontrol.wait; a no-op when nothing before it was launched this
+// way), then at once allows its own dependents to launch.  Every read of
+// an operand, an element 0 or a status comes after the wait, so the
+// ordering the stream promises is unchanged; what overlaps is launch
+// latency and CTA start-up.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Binary functor concept:
@@ -195,6 +210,7 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(EwParams p) {
   using In = typename F::In;
   using Out = typename F::Out;
   constexpr int VEC = VECTOR ? int(16 / sizeof(In)) : 1;
+  pdl_begin();
   const In* __restrict__ l = (const In*)p.l;
   const In* __restrict__ r = (const In*)p.r;
   Out* __restrict__ o = (Out*)p.o;
@@ -292,6 +308,7 @@ template <class F>
 __global__ void __launch_bounds__(kThreads) ew_tma_kernel(EwParams p) {
   using In = typename F::In;
   using Out = typename F::Out;
+  pdl_begin();
   constexpr int VEC = int(16 / sizeof(In));
   constexpr int TE = kTileBytes / int(sizeof(In));   // elements per tile
   constexpr int TV = TE / VEC;                       // 16-byte chunks per tile
@@ -399,6 +416,7 @@ __global__ void __launch_bounds__(kThreads) ew_batch_kernel(const BatchDesc* __r
   using In = typename F::In;
   using Out = typename F::Out;
   constexpr int VEC = VECTOR ? int(16 / sizeof(In)) : 1;
+  pdl_begin();
   const BatchDesc& j = jobs[blockIdx.y];
   const In* __restrict__ l = (const In*)j.l;
   const In* __restrict__ r = (const In*)j.r;
@@ -473,6 +491,27 @@ int grid_for(uint64_t work_items, const void* kernel);
 int sm_count_current();
 int tma_min_tiles_per_sm();
 bool prepare_smem(const void* kernel, int bytes);
+// CTAs of `kernel` (kThreads threads, `smem` bytes of dynamic shared
+// memory) that can be resident on one SM at once, capped at `cap`.
+int resident_per_sm(const void* kernel, int smem, int cap);
+// Whether fold kernels are launched as programmatic dependents (default
+// yes; DCF_PDL=0 turns it off).
+bool pdl_enabled();
+
+template <typename... Params, typename... Args>
+void launch_fold(void (*kernel)(Params...), dim3 grid, int smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 template <class F>
 int launch_one(const EwLaunch& a) {
@@ -485,12 +524,12 @@ int launch_one(const EwLaunch& a) {
       const uint64_t per_job = (a.n / (16 / sizeof(typename F::In))) / kUnroll;
       dim3 grid((unsigned)((per_job + kThreads - 1) / kThreads < 1 ? 1 : (per_job + kThreads - 1) / kThreads),
                 (unsigned)a.n_jobs);
-      ew_batch_kernel<F, true><<<grid, kThreads, 0, a.stream>>>(a.batch, a.flags);
+      launch_fold(ew_batch_kernel<F, true>, grid, 0, a.stream, a.batch, a.flags);
     } else {
       const uint64_t per_job = a.n / kUnroll;
       dim3 grid((unsigned)((per_job + kThreads - 1) / kThreads < 1 ? 1 : (per_job + kThreads - 1) / kThreads),
                 (unsigned)a.n_jobs);
-      ew_batch_kernel<F, false><<<grid, kThreads, 0, a.stream>>>(a.batch, a.flags);
+      launch_fold(ew_batch_kernel<F, false>, grid, 0, a.stream, a.batch, a.flags);
     }
     return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
   }
@@ -500,13 +539,16 @@ int launch_one(const EwLaunch& a) {
   if (vec && streamed > 0 && ntiles >= (uint64_t)sms * tma_min_tiles_per_sm()) {
     const int smem = kStages * kTileBytes * streamed + kStages * 8;
     if (!prepare_smem((const void*)ew_tma_kernel<F>, smem)) return DCF_ECUDA;
-    const uint64_t g = ntiles < (uint64_t)sms * kTmaCtasPerSm ? ntiles : (uint64_t)sms * kTmaCtasPerSm;
-    ew_tma_kernel<F><<<(unsigned)g, kThreads, smem, a.stream>>>(p);
+    // One wave of persistent CTAs: as many per SM as fit (at most three).
+    const int per_sm = resident_per_sm((const void*)ew_tma_kernel<F>, smem, kTmaCtasPerSm);
+    const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
+    const uint64_t g = ntiles < cap ? ntiles : cap;
+    launch_fold(ew_tma_kernel<F>, dim3((unsigned)g), smem, a.stream, p);
   } else if (vec) {
     const uint64_t items = a.n / (16 / sizeof(typename F::In));
-    ew_kernel<F, true><<<grid_for(items, (const void*)ew_kernel<F, true>), kThreads, 0, a.stream>>>(p);
+    launch_fold(ew_kernel<F, true>, dim3(grid_for(items, (const void*)ew_kernel<F, true>)), 0, a.stream, p);
   } else {
-    ew_kernel<F, false><<<grid_for(a.n, (const void*)ew_kernel<F, false>), kThreads, 0, a.stream>>>(p);
+    launch_fold(ew_kernel<F, false>, dim3(grid_for(a.n, (const void*)ew_kernel<F, false>)), 0, a.stream, p);
   }
   return cudaPeekAtLastError() == cudaSuccess ? DCF_OK : DCF_ECUDA;
 }

@@ -29,6 +29,14 @@ uint64_t launches() { return g_launches.load(std::memory_order_relaxed); }
 bool is_float(int dtype) { return dtype >= DCF_F16 && dtype <= DCF_F8E3M4; }
 bool is_int(int dtype) { return dtype >= DCF_I1 && dtype <= DCF_I64; }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("DCF_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Grid = min(blocks the work needs, blocks resident on all SMs at once).
 int grid_for(uint64_t work_items, const void* kernel) {
   static std::mutex mu;
@@ -102,8 +110,30 @@ bool prepare_smem(const void* kernel, int bytes) {
   auto it = done[dev].find(kernel);
   if (it != done[dev].end() && it->second >= bytes) return true;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  // These kernels use no L1-resident data worth keeping: give shared memory
+  // the whole carve-out, so that the pipelines' stages of several CTAs fit.
+  cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  cudaGetLastError();
   done[dev][kernel] = bytes;
   return true;
+}
+
+int resident_per_sm(const void* kernel, int smem, int cap) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::pair<int, int>> memo[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = memo[dev].find(kernel);
+  if (it != memo[dev].end() && it->second.first == smem) return it->second.second < cap ? it->second.second : cap;
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kThreads, (size_t)smem) != cudaSuccess || b < 1) {
+    cudaGetLastError();
+    b = 1;
+  }
+  memo[dev][kernel] = {smem, b};
+  return b < cap ? b : cap;
 }
 
 int launch_ew(const EwLaunch& a) {

@@ -29,8 +29,8 @@
 //     stack, so the call needs only a few hundred bytes of stack;
 //   - every operand and result pointer must be device memory of one device,
 //     and the bytes a job touches must lie inside that pointer's allocation
-//     where the driver can report it (cuMemGetAddressRange); anything else
-//     is rejected with DCF_EINVAL before any copy or launch;
+//     (one cuPointerGetAttributes per pointer); anything else is rejected
+//     with DCF_EINVAL before any copy or launch;
 //   - the caller's current device is the same on return as on entry.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -83,25 +83,43 @@ int scratch_on(DeviceSlot& slot) {
   return DCF_OK;
 }
 
-// cuMemGetAddressRange through the runtime's driver entry point (no link
-// against libcuda).  Null when the driver does not offer it.
-using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
-AddressRangeFn address_range_fn() {
-  static AddressRangeFn fn = [] {
+// cuPointerGetAttributes through the runtime's driver entry point (no link
+// against libcuda): memory type, device and allocation range of a pointer
+// in one driver call.  Null when the driver does not offer it.
+using PointerAttrsFn = CUresult (*)(unsigned, CUpointer_attribute*, void**, CUdeviceptr);
+PointerAttrsFn pointer_attrs_fn() {
+  static PointerAttrsFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+    if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      return (AddressRangeFn)p;
-    return (AddressRangeFn) nullptr;
+      return (PointerAttrsFn)p;
+    return (PointerAttrsFn) nullptr;
   }();
   return fn;
 }
 
-// Whether [p, p + bytes) is device memory of one device; that device goes
-// to *dev.  When the driver reports the allocation around p, the range
-// must lie inside it.
+// Whether [p, p + bytes) is device memory of one device, inside the
+// allocation that holds p; that device goes to *dev.
 bool device_range(const void* p, uint64_t bytes, int* dev) {
+  if (PointerAttrsFn fn = pointer_attrs_fn()) {
+    unsigned mem_type = 0;
+    int ordinal = -1;
+    CUdeviceptr start = 0;
+    size_t size = 0;
+    CUpointer_attribute attrs[4] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
+                                    CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+    void* data[4] = {&mem_type, &ordinal, &start, &size};
+    if (fn(4, attrs, data, (CUdeviceptr)(uintptr_t)p) != CUDA_SUCCESS || mem_type != CU_MEMORYTYPE_DEVICE ||
+        ordinal < 0)
+      return false;
+    *dev = ordinal;
+    if (size) {
+      const uint64_t off = (uint64_t)((uintptr_t)p - (uintptr_t)start);
+      if ((uintptr_t)p < (uintptr_t)start || off > size || bytes > size - off) return false;
+    }
+    return true;
+  }
   cudaPointerAttributes at;
   if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
     cudaGetLastError();
@@ -109,14 +127,6 @@ bool device_range(const void* p, uint64_t bytes, int* dev) {
   }
   if (at.type != cudaMemoryTypeDevice) return false;
   *dev = at.device;
-  if (AddressRangeFn fn = address_range_fn()) {
-    CUdeviceptr base = 0;
-    size_t size = 0;
-    if (fn(&base, &size, (CUdeviceptr)(uintptr_t)p) == CUDA_SUCCESS) {
-      const uint64_t off = (uint64_t)((uintptr_t)p - (uintptr_t)base);
-      if (off > size || bytes > size - off) return false;
-    }
-  }
   return true;
 }
 

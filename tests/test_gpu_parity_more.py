@@ -247,3 +247,61 @@ def test_ipowi_vs_oracle(dt, dcf, oracle):
         small = (np.arange(n) % 7).astype(a.dtype)
         for x, y in [(a, b), (small, b), (a, small), (np.where(a == 0, a.dtype.type(3), a), b)]:
             same(dcf.binary("ipowi", dt, x, y), oracle.binary("ipowi", dt, x, y), n)
+
+
+def _refusal_positions(n, te):
+    return [0, 1, te - 1, te, 7 * te + 3, n // 3, n // 2 + 1, (n // te - 1) * te, (n // te) * te - 1,
+            (n // te) * te, n - 1]
+
+
+@pytest.mark.parametrize("dt", ["i32", "i8", "i64"])
+def test_refusals_at_tile_boundaries_report_the_lowest_index(dt, dcf, oracle):
+    # The bulk-copy kernel reduces each warp's lowest refusing index and
+    # takes the minimum over all CTAs; the index it reports must be the
+    # lowest wherever the refusals are.  One zero divisor at each position
+    # (the first tile, tile boundaries, the middle, the last whole tile, the
+    # ragged tail), then zero divisors everywhere from a point on, then 1%
+    # random zeros.
+    te = 16384 // SZ[dt]
+    n = te * 1500 + 777
+    a = rbits(dt, n, 301)
+    b = rbits(dt, n, 302)
+    b = np.where(b == 0, b.dtype.type(1), b)
+    a = np.where(a == a.dtype.type(1 << (8 * SZ[dt] - 1)), a.dtype.type(5), a)   # no INT_MIN / -1
+    for pos in _refusal_positions(n, te):
+        b2 = b.copy()
+        b2[pos] = 0
+        g, c = dcf.binary("divsi", dt, a, b2), oracle.binary("divsi", dt, a, b2)
+        assert not c.folded and c.first_fail_index == pos
+        same(g, c, n)
+    for start in (0, te * 700 + 5, n - 3):
+        b2 = b.copy()
+        b2[start:] = 0
+        same(dcf.binary("remsi", dt, a, b2), oracle.binary("remsi", dt, a, b2), n)
+    b2 = b.copy()
+    b2[np.random.default_rng(5).integers(0, n, n // 100)] = 0
+    same(dcf.binary("divui", dt, a, b2), oracle.binary("divui", dt, a, b2), n)
+    # and a fold that folds, after the refusals, on the same buffers
+    same(dcf.binary("divui", dt, a, b), oracle.binary("divui", dt, a, b), n)
+
+
+def test_refused_conversion_reports_the_lowest_index_device_entry(dcf, oracle):
+    # truncf refuses at its first inexact element; through the device entry
+    # point, twice on the same status-reset buffers, and with the refusal
+    # only in the last tile.
+    import torch
+    n = 4096 * 3000 + 11
+    x = oracle.convert("extf", "f16", "f32", rbits("f16", n, 311, "nonan")).out
+    for pos in (0, n // 2, (n // 4096 - 1) * 4096 + 1, n - 1):
+        x2 = x.copy()
+        x2[pos] = np.uint32(0x3F800001)       # 1 + 2^-23: not exact in f16
+        c = oracle.convert("truncf", "f32", "f16", x2)
+        assert not c.folded and c.first_fail_index == pos
+        xt = torch.from_numpy(x2.view(np.int32)).cuda()
+        out = torch.empty(n, dtype=torch.int16, device="cuda")
+        st = torch.empty(2, dtype=torch.int64, device="cuda")
+        for _ in range(2):
+            dcf.status_reset(st)
+            dcf.convert_async("truncf", "f32", "f16", xt, out, st)
+            r = dcf.status_read(st)
+            assert (r.folded, r.first_fail_index) == (False, pos)
