@@ -51,12 +51,13 @@ typedef struct dcf_opt_stats {
 #define DCF_OPT_SPLIT_INPUT_FILE 1
 #define DCF_OPT_LOCAL_SCOPE 2
 #define DCF_OPT_DEBUGINFO 4
-/* Print every parsed constant of up to 100 elements (other than i1) through
- * the element printer (dcf_opt_print_element) instead of as its input text,
- * as the reference re-reads every dense attribute at import
- * (src/ir.rs:2149-2164).  Without it such constants keep their input text,
- * which is already in this form when mlir-opt printed the input. */
-#define DCF_OPT_REFORMAT 8
+/* By default every float and integer constant the module holds is printed
+ * from its values (dcf_opt_print_element for each element; large non-splat
+ * values as uppercase hex), as the reference re-reads every such dense
+ * attribute at import (canonical_floats, src/ir.rs:2149-2164) and prints it
+ * back.  With DCF_OPT_VERBATIM parsed constants keep their input text
+ * instead, which is the same text when mlir-opt printed the input. */
+#define DCF_OPT_VERBATIM 8
 
 int dcf_opt_run(const char* text, size_t len, const char* pipeline, int n_gpus, int flags,
                 char** out, size_t* out_len, dcf_opt_stats* stats);

@@ -84,21 +84,21 @@ def pinned_text(text):
 
 
 def run(text, pipeline: str, n_gpus: int = 1, split_input_file: bool = False, as_bytes: bool = False,
-        as_array: bool = False, local_scope: bool = False, debuginfo: bool = False, reformat: bool = False):
+        as_array: bool = False, local_scope: bool = False, debuginfo: bool = False, verbatim: bool = False):
     """Run `pipeline` over `text` (str, bytes, or a uint8 buffer such as
     pinned_text's); returns (printed module, stats dict).  The module is
     str, bytes with as_bytes=True, or with as_array=True a numpy uint8 view
     of the driver's own output buffer (no copy; freed with the array).
     local_scope prints as mlir-opt's --mlir-print-local-scope ends a module
     (no blank line after it); debuginfo prints locations, as
-    --mlir-print-debuginfo does; reformat prints parsed constants of up to
-    100 elements through the element printer (DCF_OPT_REFORMAT)."""
+    --mlir-print-debuginfo does; verbatim keeps parsed constants' input text
+    instead of printing them from their values (DCF_OPT_VERBATIM)."""
     addr, size, keep = _buffer(text)
     out = ctypes.c_void_p()
     n = ctypes.c_size_t()
     st = Stats()
     t0 = time.perf_counter()
-    rc = lib().dcf_opt_run(addr, size, pipeline.encode(), n_gpus, int(split_input_file) | (2 if local_scope else 0) | (4 if debuginfo else 0) | (8 if reformat else 0),
+    rc = lib().dcf_opt_run(addr, size, pipeline.encode(), n_gpus, int(split_input_file) | (2 if local_scope else 0) | (4 if debuginfo else 0) | (8 if verbatim else 0),
                            ctypes.byref(out),
                            ctypes.byref(n), ctypes.byref(st))
     call_ms = (time.perf_counter() - t0) * 1e3

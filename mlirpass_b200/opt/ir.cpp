@@ -483,8 +483,9 @@ class Parser {
   const std::string_view s_;
   std::string sub(size_t a, size_t n = std::string_view::npos) const { return std::string(s_.substr(a, n)); }
   Module& m_;
-  // Print parsed constants of up to 100 elements through the element
-  // printer instead of as their input text.
+  // Print parsed constants (other than big hex literals, whose uppercase
+  // hex is already their printed form) through the element printer instead
+  // of as their input text.
   const bool reformat_;
   size_t p_ = 0;
   struct Scope {
@@ -988,7 +989,7 @@ class Parser {
       memcpy(d->host.data(), &bits, d->es);
     }
     op->cst = d;
-    op->cst_text = !(reformat_ && d->n <= 100 && d->dtype != DCF_I1);
+    op->cst_text = !reformat_;
   }
 };
 

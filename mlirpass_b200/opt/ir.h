@@ -211,10 +211,12 @@ class Module {
 
 // Parse a module in MLIR's generic form.  `text` must outlive the module
 // (hex literals are decoded from it lazily).  Throws std::runtime_error.
-// reformat: constants of up to 100 elements (not i1) print through the
-// element printer, as the reference re-reads every dense attribute at
-// import (src/ir.rs:2149-2164), instead of as their input text.
-std::unique_ptr<Module> parse_module(std::string_view text, bool reformat = false);
+// reformat: parsed constants print through the element printer, as the
+// reference re-reads every float and integer dense attribute at import
+// (canonical_floats, src/ir.rs:2149-2164); otherwise they keep their input
+// text.  Big hex literals keep their text either way: uppercase hex is
+// their printed form.
+std::unique_ptr<Module> parse_module(std::string_view text, bool reformat = true);
 
 // Print the module in generic form.  Device-resident constants are fetched
 // through `fetch` (which fills DenseValue::host or returns hex digits).

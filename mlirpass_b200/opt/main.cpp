@@ -171,7 +171,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
   std::vector<dco::PrintedModule> parts;
   for (size_t i = 0; i < chunks.size(); i++) {
     auto t0 = Clock::now();
-    mods.push_back(dco::parse_module(chunks[i], (flags & DCF_OPT_REFORMAT) != 0));
+    mods.push_back(dco::parse_module(chunks[i], (flags & DCF_OPT_VERBATIM) == 0));
     dco::Module& m = *mods.back();
     total.parse_ms += ms_since(t0);
     if (i == 0 && is_pinned(text))

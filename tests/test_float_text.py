@@ -147,10 +147,12 @@ def test_random_bit_patterns_match_the_restatement(dtype):
     assert not bad, bad[:10]
 
 
-def test_folded_constants_print_as_the_fixtures_with_reformat():
+def test_folded_constants_print_as_the_fixtures():
     # Every folded golden case's expected constant, written in hex form,
-    # goes through the printer (host only, with DCF_OPT_REFORMAT): the
-    # attribute text must be exactly what mlir-opt printed in the fixture.
+    # goes through the printer (host only), which prints constants from
+    # their values as the reference does after re-reading them at import:
+    # the attribute text must be exactly what mlir-opt printed in the
+    # fixture.
     from golden_cases import CANON, SIZE, STORAGE, load_cases
     from mlir_text import parse_funcs
 
@@ -173,7 +175,8 @@ def test_folded_constants_print_as_the_fixtures_with_reformat():
             lit = ("true" if bits[0] else "false") if dt == "i1" else \
                 (("0x%0*X" % (2 * SIZE[dt], bits[0])) if isf else str(bits[0])) + f" : {ty}"
         elif dt == "i1":
-            continue                      # i1 constants are not reformatted (bit-packed raw form)
+            lit = "dense<" + ("true" if bits[0] else "false") + f"> : {ty}" if exp["splat"] else \
+                "dense<[" + ", ".join("true" if b else "false" for b in bits) + f"]> : {ty}"
         else:
             vals = bits[:1] if exp["splat"] else bits
             raw = np.array(vals, dtype=STORAGE[SIZE[dt]]).tobytes().hex().upper()
@@ -183,9 +186,9 @@ def test_folded_constants_print_as_the_fixtures_with_reformat():
                 f'  "func.func"() <{{function_type = () -> {ty}, sym_name = "t"}}> ({{\n'
                 f'    %0 = "{op}"() <{{{key} = {lit}}}> : () -> {ty}\n'
                 f'    "func.return"(%0) : ({ty}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
-        out, _ = opt.run(text, "builtin.module(func.func())", n_gpus=0, reformat=True)
+        out, _ = opt.run(text, "builtin.module(func.func())", n_gpus=0)
         f = parse_funcs(out)["t"]
         d = f.defs[f.ret.operands[0]]
         assert d.prop_map[key] == exp["text"], (c["func"], d.prop_map[key], exp["text"])
         n += 1
-    assert n >= 150
+    assert n >= 165
