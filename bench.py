@@ -649,10 +649,10 @@ def run_kernels(args):
 
 def run_profile_kernels(args):
     """One launch per round (two rounds) of the kernels profiled with ncu:
-    truncf f32->bf16, fptosi f32->i32, addi / divsi / shli i8 (the last two
-    lane-wise with a refusal mask), the batched addf of 1024
-    256x256 functions, and the 16384x16384 bf16 transpose (bulk-tensor and
-    plain-load kernels).  Operands are device-resident and larger than L2;
+    truncf f32->bf16, fptosi f32->i32, addi / divsi / shli / remsi i8 (the
+    last three lane-wise with a refusal mask), remsi i64 (32M elements), the
+    batched addf of 1024 256x256 functions, and the 16384x16384 bf16
+    transpose (bulk-tensor and plain-load kernels).  Operands are device-resident and larger than L2;
     nothing is timed here (the numbers come from the profiler)."""
     import torch
     import mlirpass_b200 as dcf
@@ -676,6 +676,9 @@ def run_profile_kernels(args):
     o8 = torch.empty(n, dtype=torch.int8, device=dev)
     wo = torch.empty_like(w)
     st = torch.empty(2, dtype=torch.int64, device=dev)
+    r64a = torch.randint(-2**62, 2**62, (n // 2,), dtype=torch.int64, device=dev, generator=g)
+    r64b = torch.randint(1, 2**62, (n // 2,), dtype=torch.int64, device=dev, generator=g)
+    o64 = torch.empty_like(r64a)
     A = [torch.rand(65536, device=dev, generator=g) for _ in range(1024)]
     B = [torch.rand(65536, device=dev, generator=g) for _ in range(1024)]
     O = [torch.empty(65536, device=dev) for _ in range(1024)]
@@ -692,6 +695,10 @@ def run_profile_kernels(args):
         dcf.binary_async("divsi", "i8", a8, d8, o8, st)
         dcf.status_reset(st)
         dcf.binary_async("shli", "i8", a8, s8, o8, st)
+        dcf.status_reset(st)
+        dcf.binary_async("remsi", "i8", a8, d8, o8, st)
+        dcf.status_reset(st)
+        dcf.binary_async("remsi", "i64", r64a, r64b, o64, st)
         dcf.status_reset(st)
         dcf.permute_async(2, (16384, 16384), (1, 0), w, wo, st)
         dcf.transpose2d_async(2, 16384, 16384, w, wo)

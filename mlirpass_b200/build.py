@@ -90,7 +90,7 @@ def build_lib(verbose: bool = False, force: bool = False) -> str:
     return LIB
 
 
-OPT_SOURCES = ["ir.cpp", "float_text.cpp", "engine.cpp", "sharded.cpp", "fold.cpp", "main.cpp"]
+OPT_SOURCES = ["ir.cpp", "float_text.cpp", "hex_host.cpp", "engine.cpp", "sharded.cpp", "fold.cpp", "main.cpp"]
 OPT_LIB = os.path.join(PKG, "libdcfold_opt.so")
 OPT_BIN = os.path.join(PKG, "dcfold-opt")
 

@@ -1,8 +1,10 @@
 // engine.cpp — see engine.h.
 #include "engine.h"
 
+#include <atomic>
 #include <chrono>
 #include <condition_variable>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <functional>
@@ -115,7 +117,7 @@ class CopyPool {
 
   CopyPool() {
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const unsigned n = std::min(15u, hw > 1 ? hw - 1 : 0u);
+    const unsigned n = std::min(63u, hw > 1 ? hw - 1 : 0u);
     for (unsigned i = 0; i < n; i++) workers_.emplace_back([this] { loop(); });
     for (auto& t : workers_) t.detach();
   }
@@ -234,9 +236,10 @@ void parallel(int n, F&& fn) {
   CopyPool::get().run(n, std::forward<F>(fn));
 }
 
-// Parts for a copy of `bytes`: about 2 MiB each, at most the pool's width.
+// Parts for a copy of `bytes`: about 512 KiB each, at most the pool's
+// width (a 16 MiB staging slot goes to every host thread).
 int parts_for(size_t bytes) {
-  const size_t p = bytes >> 21;
+  const size_t p = bytes >> 19;
   return (int)std::max<size_t>(1, std::min<size_t>(p, (size_t)CopyPool::get().width()));
 }
 
@@ -274,8 +277,11 @@ DeviceBuf::DeviceBuf(int dev, size_t n) : bytes(n), device(dev) {
   }
 }
 
+DeviceBuf::DeviceBuf(std::shared_ptr<DeviceBuf> parent, size_t offset, size_t n)
+    : ptr((char*)parent->ptr + offset), bytes(n), device(parent->device), parent_(std::move(parent)) {}
+
 DeviceBuf::~DeviceBuf() {
-  if (!ptr) return;
+  if (!ptr || parent_) return;
   Pool& p = pool();
   std::lock_guard<std::mutex> g(p.mu);
   p.free[device & 63].emplace(cap, ptr);
@@ -354,13 +360,20 @@ void Engine::download(void* dst, const void* src, size_t bytes) {
 namespace {
 
 // Copy bytes [a, b) of a packed image between its pieces and `buf`, which
-// holds image byte `a` at offset 0.  Bytes between pieces are padding.
-void copy_span(const std::vector<ImagePiece>& pcs, size_t a, size_t b, char* buf, bool to_buf) {
+// holds image byte `a` at offset 0.  Bytes between pieces are padding.  A
+// hex piece is decoded on the way in; a bad digit sets *bad.
+void copy_span(const std::vector<ImagePiece>& pcs, size_t a, size_t b, char* buf, bool to_buf,
+               std::atomic<bool>* bad) {
   auto it = std::upper_bound(pcs.begin(), pcs.end(), a,
                              [](size_t x, const ImagePiece& p) { return x < p.off + p.len; });
   for (; it != pcs.end() && it->off < b; ++it) {
     const size_t lo = std::max(a, it->off), hi = std::min(b, it->off + it->len);
     if (lo >= hi) continue;
+    if (it->hex) {
+      const char* t = (const char*)it->host + 2 * (lo - it->off);
+      if (!decode_hex_host(t, hi - lo, (uint8_t*)buf + (lo - a)) && bad) bad->store(true);
+      continue;
+    }
     char* h = (char*)it->host + (lo - it->off);
     if (to_buf) memcpy(buf + (lo - a), h, hi - lo);
     else memcpy(h, buf + (lo - a), hi - lo);
@@ -368,28 +381,42 @@ void copy_span(const std::vector<ImagePiece>& pcs, size_t a, size_t b, char* buf
 }
 
 // Split [a, a+n) of the image over host threads (one for small spans).
-void copy_slot(const std::vector<ImagePiece>& pcs, size_t a, size_t n, char* buf, bool to_buf) {
+void copy_slot(const std::vector<ImagePiece>& pcs, size_t a, size_t n, char* buf, bool to_buf,
+               std::atomic<bool>* bad = nullptr) {
   const int parts = parts_for(n);
   parallel(parts, [&](int i) {
     const size_t x = n * (size_t)i / parts, y = n * (size_t)(i + 1) / parts;
-    copy_span(pcs, a + x, a + y, buf + x, to_buf);
+    copy_span(pcs, a + x, a + y, buf + x, to_buf, bad);
   });
+}
+
+// Literal text is decoded on the host while it is staged (the default), or
+// copied as text and decoded on the GPU (DCF_OPT_DECODE=device).
+bool decode_on_host() {
+  static const bool v = [] {
+    const char* e = getenv("DCF_OPT_DECODE");
+    return !(e && std::string(e) == "device");
+  }();
+  return v;
 }
 
 size_t align16(size_t n) { return (n + 15) & ~(size_t)15; }
 
 }  // namespace
 
-// Host pieces -> pinned slots -> one contiguous device arena.
+// Host pieces -> pinned slots -> one contiguous device arena (hex pieces
+// decoded on the way).
 void Engine::upload_image(const std::vector<ImagePiece>& pcs, size_t total, char* arena) {
   ensure_pinned();
   stats.h2d_bytes += total;
   bool used[kSlots] = {false};
+  std::atomic<bool> bad{false};
   int k = 0;
   for (size_t off = 0; off < total; off += kSlotBytes) {
     const size_t n = std::min(kSlotBytes, total - off);
     if (used[k]) ck(cudaEventSynchronize(slot_ev_[k]), "cudaEventSynchronize");
-    copy_slot(pcs, off, n, (char*)pinned_[k], true);
+    copy_slot(pcs, off, n, (char*)pinned_[k], true, &bad);
+    if (bad.load()) throw std::runtime_error("invalid hex digit in a dense literal");
     ck(cudaMemcpyAsync(arena + off, pinned_[k], n, cudaMemcpyHostToDevice, s_), "H2D");
     ck(cudaEventRecord(slot_ev_[k], s_), "cudaEventRecord");
     used[k] = true;
@@ -456,8 +483,9 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
     bool is_direct;
     size_t off;
   };
-  std::vector<Loc> text, raw;
+  std::vector<Loc> text, raw, viewed;
   size_t total = 0, total_direct = 0;
+  const bool host_decode = decode_on_host();
   for (DenseValue* v : vs) {
     if (v->poison) throw std::runtime_error("a poison value has no bytes");
     if (!v->host.empty() && PinnedPool::get().owned(v->host.data())) {
@@ -466,7 +494,13 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
       total_direct = align16(total_direct + v->bytes());
     } else if (!v->host.empty()) {
       staged.push_back({(void*)v->host.data(), nullptr, v->bytes(), total});
-      raw.push_back({v, false, total});
+      (host_decode ? viewed : raw).push_back({v, false, total});
+      total = align16(total + v->bytes());
+    } else if (!v->hex.empty() && host_decode) {
+      // Decoded into the staging slots: raw bytes cross PCIe, and the
+      // constant is a view of the arena (no device-side decode or copy).
+      staged.push_back({(void*)v->hex.data(), nullptr, v->bytes(), total, true});
+      viewed.push_back({v, false, total});
       total = align16(total + v->bytes());
     } else if (!v->hex.empty() && in_pinned(v->hex.data(), v->hex.size())) {
       text.push_back({v, true, 0});  // placed below, with its neighbours in the input
@@ -479,7 +513,12 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
     }
   }
   std::vector<std::shared_ptr<DeviceBuf>> bufs(vs.size());
-  for (size_t i = 0; i < vs.size(); i++) bufs[i] = std::make_shared<DeviceBuf>(dev_, vs[i]->bytes());
+  {
+    std::vector<bool> is_view(vs.size(), false);
+    for (const Loc& l : viewed) is_view[index.at(l.v)] = true;
+    for (size_t i = 0; i < vs.size(); i++)
+      if (!is_view[i]) bufs[i] = std::make_shared<DeviceBuf>(dev_, vs[i]->bytes());
+  }
   auto buf_of = [&](DenseValue* v) -> std::shared_ptr<DeviceBuf>& { return bufs[index.at(v)]; };
   // Literals inside the page-locked input are copied as runs: literals whose
   // gaps in the input are short go in one copy with the text between them,
@@ -512,7 +551,8 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
       l->off = runs.back().off + (size_t)(l->v->hex.data() - runs.back().a);
     }
   }
-  std::unique_ptr<DeviceBuf> arena, arena_direct;
+  std::shared_ptr<DeviceBuf> arena;
+  std::unique_ptr<DeviceBuf> arena_direct;
   if (!direct.empty() || !runs.empty()) {
     arena_direct = std::make_unique<DeviceBuf>(dev_, total_direct + 32);
     for (const ImagePiece& p : direct)
@@ -525,8 +565,9 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
     for (const ImagePiece& p : direct) stats.h2d_bytes += p.len;
   }
   if (total) {
-    arena = std::make_unique<DeviceBuf>(dev_, total);
+    arena = std::make_shared<DeviceBuf>(dev_, total);
     upload_image(staged, total, (char*)arena->ptr);
+    for (const Loc& l : viewed) buf_of(l.v) = std::make_shared<DeviceBuf>(arena, l.off, l.v->bytes());
   }
   auto at = [&](const Loc& l) {
     return (const char*)(l.is_direct ? arena_direct->ptr : arena->ptr) + l.off;

@@ -26,6 +26,9 @@ namespace dco {
 class DeviceBuf {
  public:
   DeviceBuf(int device, size_t bytes);
+  // A view of `bytes` bytes at `offset` inside `parent` (which it keeps
+  // alive): the constants of one packed upload share their arena.
+  DeviceBuf(std::shared_ptr<DeviceBuf> parent, size_t offset, size_t bytes);
   ~DeviceBuf();
   DeviceBuf(const DeviceBuf&) = delete;
   DeviceBuf& operator=(const DeviceBuf&) = delete;
@@ -33,6 +36,9 @@ class DeviceBuf {
   size_t bytes = 0;
   size_t cap = 0;
   int device = 0;
+
+ private:
+  std::shared_ptr<DeviceBuf> parent_;
 };
 
 // One element-level fold.  The greedy driver fills the inputs; the engine
@@ -66,7 +72,12 @@ struct ImagePiece {
   void* host;         // source (upload) or destination (download)
   const void* dev;    // device source of a download
   size_t len, off;    // bytes, offset in the image
+  bool hex = false;   // upload: `host` is hex text of 2 * len characters, decoded on the way
 };
+
+// Decode `nbytes` bytes from 2 * nbytes hex characters (either case) on the
+// host; false if any character is not a hex digit.  Thread-safe.
+bool decode_hex_host(const char* in, size_t nbytes, uint8_t* out);
 
 struct EngineStats {
   uint64_t h2d_bytes = 0, d2h_bytes = 0, requests = 0, batches = 0;
