@@ -23,7 +23,8 @@ folds of 16,777,216 elements, 192 MiB of algorithmic traffic each (two
          run.  Every printed module is checked against the expected results
          (tests/golden/config_digests.json) before the line is printed;
   pass_config5  configuration 5 (4096 functions + the 16384^2 bf16
-         transpose, 5.4 GB of text) through
+         transpose, 5.4 GB of text in page-locked memory; the pageable
+         figure beside it) through
          builtin.module(func.func(tosa-layerwise-constant-fold,canonicalize)),
          same timing and check;
   cpu_baseline  the oracle (the scalar C restatement of the reference's
@@ -255,11 +256,11 @@ def pass_runs(opt, text, pipeline, n_gpus, warmup, steps, config):
     return runs, ok
 
 
-def pass_summary(runs, algo_bytes, config, pipeline, text_bytes, n_gpus, ok):
+def pass_summary(runs, algo_bytes, config, pipeline, text_bytes, n_gpus, ok, memory="pageable"):
     mean = lambda k: statistics.mean(s[k] for s in runs)
     run_ms = mean("run_ms")
     return {"config": config, "pipeline": pipeline, "n_gpus": n_gpus, "text_bytes": text_bytes,
-            "text_memory": "pageable", "runs": len(runs),
+            "text_memory": memory, "runs": len(runs),
             "run_ms": round(run_ms, 3), "run_ms_best": round(min(s["run_ms"] for s in runs), 3),
             "call_ms": round(mean("call_ms"), 2), "parse_ms": round(mean("parse_ms"), 2),
             "print_ms": round(mean("print_ms"), 2), "upload_ms": round(mean("upload_ms"), 2),
@@ -351,20 +352,28 @@ def run_gpu(args):
     kernel_ms_max = allreduce_max(kernel_ms, world)
 
     # ---- e2e: the whole configuration through the pass driver, from its MLIR
-    # text in pageable host memory; rank 0 drives all `world` GPUs (the
-    # module's constants split into one element range per GPU) while the
-    # other ranks wait on the host.
-    e2e = p5 = None
+    # text in pageable host memory (and, as a second figure, in page-locked
+    # memory); rank 0 drives all `world` GPUs (the module's constants split
+    # into one element range per GPU) while the other ranks wait on the host.
+    e2e = e2e_pinned = p5 = p5_pageable = None
     launches1 = dcf.kernel_launches()
     if rank == 0:
         text2 = G.config2_module().tobytes()
         runs2, ok2 = pass_runs(opt, text2, "canonicalize", world, args.warmup, args.steps, "config2")
         e2e = pass_summary(runs2, STEP_BYTES, "config2", "canonicalize", len(text2), world, ok2)
-        del text2
+        pin2 = opt.pinned_text(text2)
+        runs2p, ok2p = pass_runs(opt, pin2, "canonicalize", world, args.warmup, args.steps, "config2")
+        e2e_pinned = pass_summary(runs2p, STEP_BYTES, "config2", "canonicalize", len(text2), world, ok2p, "pinned")
+        del text2, pin2
         if not args.no_config5:
             text5 = G.config5_module(4096).tobytes()
-            runs5, ok5 = pass_runs(opt, text5, G.LAYERWISE, world, 1, max(1, min(args.steps, 3)), "config5")
-            p5 = pass_summary(runs5, CONFIG5_BYTES, "config5", G.LAYERWISE, len(text5), world, ok5)
+            reps = max(1, min(args.steps, 3))
+            pin5 = opt.pinned_text(text5)
+            runs5, ok5 = pass_runs(opt, pin5, G.LAYERWISE, world, 1, reps, "config5")
+            p5 = pass_summary(runs5, CONFIG5_BYTES, "config5", G.LAYERWISE, len(text5), world, ok5, "pinned")
+            del pin5
+            runs5q, ok5q = pass_runs(opt, text5, G.LAYERWISE, world, 1, reps, "config5")
+            p5_pageable = pass_summary(runs5q, CONFIG5_BYTES, "config5", G.LAYERWISE, len(text5), world, ok5q)
             del text5
     pass_launches = dcf.kernel_launches() - launches1
     wait_for_rank0(world, rank, "pass_done")
@@ -428,11 +437,13 @@ def run_gpu(args):
                         "reference's bench times it; the printed module is checked against the expected "
                         "results every run",
                 "pass": e2e,
+                "pinned_text": e2e_pinned,
                 "c_abi_pinned": {"value": round(STEP_BYTES / (cabi_ms_max * 1e-3) / 1e9, 2), "unit": "GB/s",
                                  "ms_per_step": round(cabi_ms_max, 3),
                                  "path": "dcf_binary (host C ABI) on raw operands in pinned host buffers, this "
                                          "rank's rows, 6 calls per step"}},
         "pass_config5": p5,
+        "pass_config5_pageable": p5_pageable,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "ew_tma_kernel<FArith/FMinMax f32>: cp.async.bulk 16 KB tiles, 2 stages, "
