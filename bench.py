@@ -298,19 +298,20 @@ def run_gpu(args):
     flush = torch.ones(32 << 20, dtype=torch.int64, device=dev)   # 256 MiB (L2 is 126 MB)
     stream = torch.cuda.current_stream(dev)
 
-    def chain(fold_events=None, read_flush=False):
+    def chain(fold_events=None, read_flush=False, on=None):
+        on = on or stream
         if not read_flush:
             status.fill_(-1)          # the six statuses at once (all bytes 0xFF)
         for i, (op, a, b, t) in enumerate(CHAIN):
             st = status[2 * i:2 * i + 2]
             if read_flush:
                 flush.sum()
-                dcf.status_reset(st, stream)
+                dcf.status_reset(st, on)
             if fold_events is not None:
-                fold_events[i][0].record(stream)
-            dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=n, stream=stream)
+                fold_events[i][0].record(on)
+            dcf.binary_async(op, "f32", res[a], res[b], res[t], st, n=n, stream=on)
             if fold_events is not None:
-                fold_events[i][1].record(stream)
+                fold_events[i][1].record(on)
 
     for _ in range(args.warmup):
         chain(read_flush=True)
@@ -319,6 +320,26 @@ def run_gpu(args):
         r = dcf.status_read(status[2 * i:2 * i + 2], stream)
         if not r.folded:
             raise SystemExit(f"fold {CHAIN[i][0]} refused at {r.first_fail_index}")
+
+    # The step's six launches are captured once in a CUDA graph and replayed:
+    # at small per-GPU sizes (2M elements at 8 GPUs, ~7 us a fold) the host
+    # cannot issue launches as fast as the GPU runs them.
+    graph = None
+    if not args.no_graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(stream)
+            with torch.cuda.graph(g, stream=cap):
+                chain(on=cap)
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            graph = g
+        except Exception as e:  # noqa: BLE001 - fall back to launching from the host
+            sys.stderr.write(f"graph capture of the chain failed ({e}); launching from the host\n")
+            torch.cuda.synchronize()
+    step = graph.replay if graph is not None else chain
 
     clocks = Clocks(local)
     clocks.start()
@@ -331,7 +352,7 @@ def run_gpu(args):
     for s in range(args.steps):
         flush.add_(1)
         step_ev[s][0].record(stream)
-        chain()
+        step()
         step_ev[s][1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -342,7 +363,7 @@ def run_gpu(args):
         chain(fold_ev[s], read_flush=True)
     torch.cuda.synchronize()
     barrier(world)
-    value_launches = dcf.kernel_launches() - launches0
+    value_launches = dcf.kernel_launches() - launches0 + (len(CHAIN) * args.steps if graph is not None else 0)
     fold_ms = [[fold_ev[s][i][0].elapsed_time(fold_ev[s][i][1]) for i in range(len(CHAIN))]
                for s in range(args.steps)]
     kernel_ms = sum(sum(x) for x in fold_ms) / (args.steps * len(CHAIN))
@@ -456,7 +477,8 @@ def run_gpu(args):
                      "kernel_ms": round(kernel_ms_max, 5), "per_fold_us": per_fold_us,
                      "bytes_per_launch": fold_bytes},
         "gpu_launches": int(launches),
-        "gpu_launches_detail": {"value_and_roofline": int(value_launches), "pass_runs": int(pass_launches),
+        "gpu_launches_detail": {"value_and_roofline": int(value_launches), "value_launch": "CUDA graph replay"
+                                if graph is not None else "host launches", "pass_runs": int(pass_launches),
                                 "c_abi": int(cabi_launches)},
         "clocks": clk,
     }
@@ -869,6 +891,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config5", action="store_true", help="skip the config 5 pass runs of the default line")
+    ap.add_argument("--no-graph", action="store_true", help="launch the value steps from the host, not a CUDA graph")
     ap.add_argument("--workload", default="chain4096",
                     help="chain4096 (the headline line), kernels, profile-kernels, h2d (host<->device copy "
                          "ceiling of --gpus GPUs at once), or pass:<config1|config2|config3-i8|...|config5>")

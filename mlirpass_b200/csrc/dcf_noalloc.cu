@@ -29,8 +29,9 @@
 //     stack, so the call needs only a few hundred bytes of stack;
 //   - every operand and result pointer must be device memory of one device,
 //     and the bytes a job touches must lie inside that pointer's allocation
-//     (one cuPointerGetAttributes per pointer); anything else is rejected
-//     with DCF_EINVAL before any copy or launch;
+//     (one cuPointerGetAttributes per allocation and call: ranges inside an
+//     allocation already checked in the call need none); anything else is
+//     rejected with DCF_EINVAL before any copy or launch;
 //   - the caller's current device is the same on return as on entry.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -99,9 +100,36 @@ PointerAttrsFn pointer_attrs_fn() {
   return fn;
 }
 
+// Allocations already checked within one call: jobs often point into the
+// same allocation (a caching allocator's segment, an upload arena), and a
+// range inside one of these needs no driver call.
+struct RangeCache {
+  static constexpr int kSlots = 8;
+  uintptr_t start[kSlots] = {0};
+  uint64_t size[kSlots] = {0};
+  int dev[kSlots] = {0};
+  int next = 0;
+  bool find(const void* p, uint64_t bytes, int* d) const {
+    const uintptr_t a = (uintptr_t)p;
+    for (int k = 0; k < kSlots; k++)
+      if (size[k] && a >= start[k] && a - start[k] <= size[k] && bytes <= size[k] - (a - start[k])) {
+        *d = dev[k];
+        return true;
+      }
+    return false;
+  }
+  void add(uintptr_t s, uint64_t n, int d) {
+    start[next] = s;
+    size[next] = n;
+    dev[next] = d;
+    next = (next + 1) % kSlots;
+  }
+};
+
 // Whether [p, p + bytes) is device memory of one device, inside the
 // allocation that holds p; that device goes to *dev.
-bool device_range(const void* p, uint64_t bytes, int* dev) {
+bool device_range(const void* p, uint64_t bytes, int* dev, RangeCache& cache) {
+  if (cache.find(p, bytes, dev)) return true;
   if (PointerAttrsFn fn = pointer_attrs_fn()) {
     unsigned mem_type = 0;
     int ordinal = -1;
@@ -117,6 +145,7 @@ bool device_range(const void* p, uint64_t bytes, int* dev) {
     if (size) {
       const uint64_t off = (uint64_t)((uintptr_t)p - (uintptr_t)start);
       if ((uintptr_t)p < (uintptr_t)start || off > size || bytes > size - off) return false;
+      cache.add((uintptr_t)start, size, ordinal);
     }
     return true;
   }
@@ -172,6 +201,7 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
   DeviceRestore restore;
   if (dev >= 0 && cudaSetDevice(dev) != cudaSuccess) return noalloc_fail(DCF_ECUDA, "cudaSetDevice failed");
   // Validate every job before any copy or launch.
+  RangeCache checked;
   for (size_t i = 0; i < n_jobs; i++) {
     dcf_job& j = jobs[i];
     memset(&j.result, 0, sizeof j.result);
@@ -200,8 +230,9 @@ extern "C" int dcf_batch_noalloc(dcf_job* jobs, size_t n_jobs, void* stream) {
     const uint64_t es = dtype_size((int)j.dtype), oes = dtype_size((int)j.out_dtype);
     if (j.n > (UINT64_MAX >> 4)) return noalloc_fail(DCF_EINVAL, "a job's element count is too large");
     int d_out = -1, d_l = -1, d_r = -1;
-    if (!device_range(j.out, j.n * oes, &d_out) || !device_range(j.lhs, j.lhs_splat ? es : j.n * es, &d_l) ||
-        (bin && !device_range(j.rhs, j.rhs_splat ? es : j.n * es, &d_r)))
+    if (!device_range(j.out, j.n * oes, &d_out, checked) ||
+        !device_range(j.lhs, j.lhs_splat ? es : j.n * es, &d_l, checked) ||
+        (bin && !device_range(j.rhs, j.rhs_splat ? es : j.n * es, &d_r, checked)))
       return noalloc_fail(DCF_EINVAL,
                           "dcf_batch_noalloc needs device buffers that hold each job's operands and result");
     if (d_out != dev || d_l != dev || (bin && d_r != dev))

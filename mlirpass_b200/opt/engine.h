@@ -121,16 +121,13 @@ class Engine {
   EngineStats stats;
 
   // Host memory the copy engine can read directly (page-locked input
-  // text).  With decode_on_host its literals are decoded by host threads
-  // into the staging slots like any other text (one GPU: the host cores
-  // keep up with one link, and half the bytes cross it); otherwise they
-  // are copied straight from there as text and decoded on the GPU (several
-  // GPUs: the copy engines move the text without the host cores, which
-  // decoding for every GPU at once would saturate).
-  void set_pinned_source(const void* begin, size_t bytes, bool decode_on_host) {
+  // text): its literals are copied straight from there as text and decoded
+  // on the GPU, with no host core touching them.  (Decoding them on the
+  // host instead halves the bytes over PCIe but was slower on every
+  // configuration but one at one GPU, and CPU-bound at eight.)
+  void set_pinned_source(const void* begin, size_t bytes) {
     pinned_src_ = (const char*)begin;
     pinned_len_ = bytes;
-    pinned_host_decode_ = decode_on_host;
   }
 
   // Device -> host copy of `bytes` (synchronous).  Large copies to
@@ -142,7 +139,6 @@ class Engine {
   int dev_;
   cudaStream_t s_ = nullptr;
   const char* pinned_src_ = nullptr;
-  bool pinned_host_decode_ = true;
   size_t pinned_len_ = 0;
   bool in_pinned(const void* p, size_t n) const {
     return pinned_src_ && (const char*)p >= pinned_src_ && (const char*)p + n <= pinned_src_ + pinned_len_;
