@@ -30,7 +30,7 @@ GEN_LIB = os.path.join(PKG, "libdcfgen.so")
 SOURCES = ["dcf_ew_float.cu", "dcf_ew_float_f32.cu", "dcf_ew_float_f64.cu", "dcf_ew_float_h.cu",
            "dcf_ew_float_f8.cu", "dcf_ew_int.cu", "dcf_ew_convert.cu", "dcf_ew_convert_ff.cu",
            "dcf_ew_convert_if.cu", "dcf_ew_convert_fi.cu", "dcf_ew_math.cu", "dcf_misc.cu", "dcf_transpose_tma.cu", "dcf_runtime.cu",
-           "dcf_noalloc.cu"]
+           "dcf_noalloc.cu", "dcf_rt.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -102,13 +102,14 @@ def _cuda_home() -> str:
 def build_opt(force: bool = False) -> list[str]:
     """The pass driver: libdcfold_opt.so and the dcfold-opt executable."""
     srcs = [os.path.join(PKG, "opt", f) for f in OPT_SOURCES]
-    deps = srcs + [os.path.join(PKG, "opt", f) for f in ("ir.h", "engine.h", "fold.h")] + \
+    deps = srcs + [os.path.join(PKG, "opt", f) for f in ("ir.h", "engine.h", "fold.h", "cuda_rt.h")] + \
         [os.path.join(ROOT, "include", "dcfold.h"), os.path.join(ROOT, "include", "dcfold_opt.h"), LIB]
     cuda = _cuda_home()
     cxx = os.environ.get("CXX", "g++")
     common = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-I", os.path.join(cuda, "include")]
-    link = ["-L", PKG, "-ldcfold", "-Wl,-rpath,$ORIGIN", "-L", os.path.join(cuda, "lib64"),
-            "-lcudart_static", "-lpthread", "-ldl", "-lrt"]
+    # No CUDA runtime of its own: the driver's runtime calls go through
+    # libdcfold.so's (opt/cuda_rt.h), one runtime per process.
+    link = ["-L", PKG, "-ldcfold", "-Wl,-rpath,$ORIGIN", "-lpthread", "-ldl", "-lrt"]
     out = []
     for target, extra in ((OPT_LIB, ["-shared"]), (OPT_BIN, ["-DDCFOLD_OPT_MAIN"])):
         if force or _stale(target, deps):

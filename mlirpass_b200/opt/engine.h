@@ -9,7 +9,7 @@
 // kept as one host-side element, as MLIR stores a splat.
 #pragma once
 
-#include <cuda_runtime.h>
+#include "cuda_rt.h"
 
 #include <memory>
 #include <string>
