@@ -496,7 +496,9 @@ void Engine::to_device_all(const std::vector<DenseValue*>& in) {
       staged.push_back({(void*)v->host.data(), nullptr, v->bytes(), total});
       (host_decode ? viewed : raw).push_back({v, false, total});
       total = align16(total + v->bytes());
-    } else if (!v->hex.empty() && host_decode && !in_pinned(v->hex.data(), v->hex.size())) {
+    } else if (!v->hex.empty() && host_decode &&
+               (!in_pinned(v->hex.data(), v->hex.size()) ||
+                (pinned_small_on_host_ && v->hex.size() < kSmallPinnedHex))) {
       // Pageable text (which the host must copy anyway) is decoded into the
       // staging slots: raw bytes cross PCIe, and the constant is a view of
       // the arena (no device-side decode or copy).

@@ -122,12 +122,18 @@ class Engine {
 
   // Host memory the copy engine can read directly (page-locked input
   // text): its literals are copied straight from there as text and decoded
-  // on the GPU, with no host core touching them.  (Decoding them on the
-  // host instead halves the bytes over PCIe but was slower on every
-  // configuration but one at one GPU, and CPU-bound at eight.)
-  void set_pinned_source(const void* begin, size_t bytes) {
+  // on the GPU, with no host core touching them.  With small_on_host (one
+  // GPU in the run), literals of less than kSmallPinnedHex characters are
+  // decoded by the host threads instead, as pageable text is: measured on
+  // one B200, config 5's 8192 literals of 512 KB ran 183 ms that way
+  // against 216 ms, while config 2's 134 MB literals ran 12.6 ms on the
+  // device against 16.1 ms; with several GPUs decoding on the host for all
+  // of them was CPU-bound (config 5 at 8 GPUs: 103 against 64 ms).
+  static constexpr size_t kSmallPinnedHex = 4u << 20;
+  void set_pinned_source(const void* begin, size_t bytes, bool small_on_host) {
     pinned_src_ = (const char*)begin;
     pinned_len_ = bytes;
+    pinned_small_on_host_ = small_on_host;
   }
 
   // Device -> host copy of `bytes` (synchronous).  Large copies to
@@ -139,6 +145,7 @@ class Engine {
   int dev_;
   cudaStream_t s_ = nullptr;
   const char* pinned_src_ = nullptr;
+  bool pinned_small_on_host_ = false;
   size_t pinned_len_ = 0;
   bool in_pinned(const void* p, size_t n) const {
     return pinned_src_ && (const char*)p >= pinned_src_ && (const char*)p + n <= pinned_src_ + pinned_len_;

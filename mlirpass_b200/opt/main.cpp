@@ -175,7 +175,7 @@ Output run_all(std::string_view text, const std::string& pipeline, int n_gpus, i
     dco::Module& m = *mods.back();
     total.parse_ms += ms_since(t0);
     if (i == 0 && is_pinned(text))
-      for (auto& e : eng.own) e->set_pinned_source(text.data(), text.size());
+      for (auto& e : eng.own) e->set_pinned_source(text.data(), text.size(), eng.list.size() == 1);
     t0 = Clock::now();
     dco::PassStats ps;
     std::vector<dco::Engine*> engines = eng.for_pipeline(pipeline);
