@@ -563,7 +563,7 @@ def run_reference(args):
     gbs = STEP_BYTES / (ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64-seeded dense constants; no dataset)",
         "config": dict(CONFIG, parallelism="host threads over row blocks (one process)"),
         "impl": "reference",

@@ -192,3 +192,13 @@ def test_folded_constants_print_as_the_fixtures():
         assert d.prop_map[key] == exp["text"], (c["func"], d.prop_map[key], exp["text"])
         n += 1
     assert n >= 165
+
+
+def test_print_element_rejects_other_types_and_short_buffers():
+    L = opt.lib()
+    L.dcf_opt_print_element.argtypes = [ctypes.c_int, ctypes.c_ulonglong, ctypes.c_char_p, ctypes.c_size_t]
+    buf = ctypes.create_string_buffer(4)
+    assert L.dcf_opt_print_element(99, 0, buf, 4) < 0
+    assert L.dcf_opt_print_element(DTYPES["f32"], 0x3F800000, buf, 4) < 0     # "1.000000e+00" needs 13 bytes
+    assert L.dcf_opt_print_element(DTYPES["i8"], 0xFF, buf, 4) == 2 and buf.value == b"-1"
+    assert printed("i1", 1) == "true" and printed("i64", (1 << 64) - 5) == "-5"

@@ -506,3 +506,34 @@ def check_resource_operands_stay(n_gpus):
 
 def test_dense_resource_operands_are_not_folded():
     check_resource_operands_stay(1)
+
+
+@pytest.mark.parametrize("memory", ["pageable", "pinned"])
+@pytest.mark.parametrize("n", [1 << 12, 1 << 21])
+def test_literals_with_a_bad_hex_digit_are_rejected(memory, n):
+    # A literal body with a character that is not a hex digit is an error,
+    # whichever decoder reads it: the host threads (pageable text, and small
+    # page-locked literals at one GPU) or the device (large page-locked
+    # literals); lower-case digits are accepted.
+    T = f"tensor<{n}xf32>"
+    good = np.arange(n, dtype=np.float32)
+    h = _hex(good.view(np.uint32))
+    fm = "<{fastmath = #arith.fastmath<none>}>"
+
+    def module(body):
+        return ('"builtin.module"() ({\n'
+                f'  "func.func"() <{{function_type = () -> {T}, sym_name = "main"}}> ({{\n'
+                f'    %a = "arith.constant"() <{{value = dense<"0x{body}"> : {T}}}> : () -> {T}\n'
+                f'    %b = "arith.constant"() <{{value = dense<"0x{h}"> : {T}}}> : () -> {T}\n'
+                f'    %0 = "arith.addf"(%a, %b) {fm} : ({T}, {T}) -> {T}\n'
+                f'    "func.return"(%0) : ({T}) -> ()\n  }}) : () -> ()\n}}) : () -> ()\n')
+
+    src = (lambda t: t) if memory == "pageable" else opt.pinned_text
+    out, st = opt.run(src(module(h.lower())), "canonicalize")
+    (d,) = consts_returned(out)
+    assert st["folds"] == 1 and np.array_equal(full(d, n), (good + good).view(np.uint32).astype(np.uint64))
+    for pos in (0, len(h) // 2 + 1, len(h) - 1):
+        bad = h[:pos] + "G" + h[pos + 1:]
+        with pytest.raises(opt.OptError) as e:
+            opt.run(src(module(bad)), "canonicalize")
+        assert "hex" in str(e.value)
