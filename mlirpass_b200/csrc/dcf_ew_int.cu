@@ -18,28 +18,87 @@ template <int OP, int W> constexpr bool checked_word_op() {
                                  OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI);
 }
 
-// floor(x / d) for 0 <= x < 2^16 and 1 <= d < 2^16 on the FMA and integer
-// pipes only: no division, no reciprocal unit and no int<->float conversion
-// instruction (those run on the narrow transcendental / conversion unit,
-// which limited the lane-wise 8-bit division).  The operands become floats
-// exactly by the magic-number trick (2^23 + v has v as its low mantissa
-// bits); the reciprocal starts from the exponent-negation seed of the fast
-// inverse methods (e.g. C. Lomont, "Fast Inverse Square Root", 2003, whose
-// reciprocal form is within 12.5% of 1/d) and takes STEPS Newton-Raphson
-// steps r <- r + r (1 - d r), each squaring the relative error (2 steps:
-// < 2.5e-4, enough for x < 2^8; 3 steps: < 1e-7 with f32 rounding, enough
-// for x < 2^16), so x * r rounded to an integer is floor(x / d) or one more,
-// and one integer correction makes it exact.
-template <int STEPS>
-__device__ __forceinline__ uint32_t udiv_small(uint32_t x, uint32_t d) {
-  const float xf = __int_as_float(0x4B000000u | x) - 8388608.0f;
-  const float df = __int_as_float(0x4B000000u | d) - 8388608.0f;
-  float r = __int_as_float(0x7EF311C3 - __float_as_int(df));
+// 1/d for an integer 1 <= d < 2^16 (as a float), as accurate as a lane
+// division of width W needs (below).  The start is the exponent-negation
+// seed of the fast inverse methods (e.g. C. Lomont, "Fast Inverse Square
+// Root", 2003): r0 = bits(0x7EF311C3 - bits(d)), whose relative error
+// e0 = 1 - d r0 is at most 0.0506 over these integers (up to 12.5% only
+// for mantissas no integer below 2^16 has).  A Newton-Raphson step
+// r <- r + r e (e = 1 - d r) squares the error and costs two FMAs; the
+// cubic step r <- r + r (e + e^2) cubes it and costs three.
+//   8-bit signed (|x| <= 2^7):     one Newton step, |e| < 2.6e-3
+//   8-bit unsigned (x < 2^8):      one cubic step,  |e| < 1.3e-4
+//   16-bit signed (|x| <= 2^15):   two Newton steps, |e| < 6.6e-6
+//   16-bit unsigned (x < 2^16):    cubic + Newton,  |e| < 2e-7 (f32 rounding)
+template <int W, bool kSigned>
+__device__ __forceinline__ float lane_recip(float d) {
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(d));
+  const float e = __fmaf_rn(-d, r, 1.0f);
+  if constexpr (kSigned) {
+    r = __fmaf_rn(r, e, r);
+    if constexpr (W == 16) r = __fmaf_rn(r, __fmaf_rn(-d, r, 1.0f), r);
+  } else {
+    r = __fmaf_rn(r, __fmaf_rn(e, e, e), r);
+    if constexpr (W == 16) r = __fmaf_rn(r, __fmaf_rn(-d, r, 1.0f), r);
+  }
+  return r;
+}
+
+// Quotients and remainders of all 8- or 16-bit lanes of a 32-bit word on
+// the FMA pipe, with no division, reciprocal or int<->float conversion
+// instruction (those run on the narrow conversion unit) and few integer
+// instructions (the integer ALU pipe limited the lane-by-lane form).
+//  - Each lane becomes an exact float by the magic-number trick: one byte
+//    permutation puts the lane under the exponent of 2^23, so the float is
+//    2^23 + v.  Signed lanes are biased by 2^(W-1) first (an xor on the
+//    whole word) and unbiased in the same subtraction; unsigned dividends
+//    come out as x + 1/2 from it.
+//  - floor(|x| / |d|) = floor((|x| + 1/2) r) with r = lane_recip(|d|):
+//    (|x| + 1/2) / |d| lies at least 1/(2|d|) away from every integer, and
+//    the error (|x| + 1/2) e / |d| stays below that while
+//    (|x| + 1/2) |e| < 1/2, which the accuracy of lane_recip gives for each
+//    width.  One fma rounded toward zero onto the 2^23 grid takes the floor
+//    exactly: no integer correction step.
+//  - The remainder |x| - q |d| is exact in f32; truncating signed division
+//    gives the quotient the sign of x d and the remainder the sign of x.
+//  - Each result v lands in the low mantissa bits of v + 2^23 (+ 2^W for
+//    signed lanes, whose v may be negative) and byte permutations pack the
+//    lanes back.
+// b must hold no zero lane.
+template <int OP, int W>
+__device__ __forceinline__ uint32_t div_lanes(uint32_t a, uint32_t b) {
+  constexpr bool kSigned = OP == DCF_DIVSI || OP == DCF_REMSI;
+  constexpr bool kRem = OP == DCF_REMSI || OP == DCF_REMUI;
+  constexpr uint32_t kBias = kSigned ? (W == 8 ? 0x80808080u : 0x80008000u) : 0u;
+  constexpr float kMagic = 8388608.0f;  // 2^23
+  constexpr float kDOff = kMagic + (kSigned ? (float)(1u << (W - 1)) : 0.0f);
+  constexpr float kXOff = kSigned ? kDOff : kMagic - 0.5f;
+  constexpr float kWrap = kSigned ? kMagic + (float)(1u << W) : kMagic - 0.5f;
+  a ^= kBias;
+  b ^= kBias;
+  uint32_t f[32 / W];
 #pragma unroll
-  for (int i = 0; i < STEPS; i++) r = __fmaf_rn(r, __fmaf_rn(-df, r, 1.0f), r);
-  uint32_t q = (uint32_t)__float_as_int(__fmaf_rn(xf, r, 8388608.0f)) - 0x4B000000u;
-  if ((int32_t)(x - q * d) < 0) q--;
-  return q;
+  for (int k = 0; k < 32 / W; k++) {
+    const uint32_t sel = W == 8 ? (0x7440u | k) : (0x7400u | ((2u * k + 1) << 4) | (2u * k));
+    const float x = __int_as_float(__byte_perm(a, 0x4B000000u, sel)) - kXOff;  // unsigned: x + 1/2
+    const float d = __int_as_float(__byte_perm(b, 0x4B000000u, sel)) - kDOff;
+    const float ad = kSigned ? fabsf(d) : d;
+    const float xh = kSigned ? fabsf(x) + 0.5f : x;
+    const float qm = __fmaf_rz(xh, lane_recip<W, kSigned>(ad), kMagic);  // 2^23 + floor(|x| / |d|)
+    if constexpr (OP == DCF_DIVUI) {
+      f[k] = __float_as_uint(qm);
+    } else if constexpr (OP == DCF_REMUI) {
+      f[k] = __float_as_uint(__fmaf_rn(-(qm - kMagic), ad, xh) + kWrap);
+    } else {
+      const float q = qm - kMagic;
+      const float v = kRem ? copysignf(__fmaf_rn(-q, ad, fabsf(x)), x) : copysignf(q, x * d);
+      f[k] = __float_as_uint(v + kWrap);
+    }
+  }
+  if constexpr (W == 8)
+    return __byte_perm(__byte_perm(f[0], f[1], 0x0040u), __byte_perm(f[2], f[3], 0x0040u), 0x5410u);
+  else
+    return __byte_perm(f[0], f[1], 0x5410u);
 }
 
 template <int OP, int W> struct IOp {
@@ -51,45 +110,38 @@ template <int OP, int W> struct IOp {
   // Lane by lane in registers, with the refusals of all lanes found at
   // once (the returned mask): a shift amount of the width or more, a zero
   // divisor, and the signed minimum divided by -1; a refusing lane still
-  // gets some value, which is never used.  Quotients of 8- and 16-bit
-  // lanes come from udiv_small on the magnitudes (truncating division of
-  // signed lanes: the magnitude of the quotient, then its sign).
+  // gets some value, which is never used.  Quotients and remainders come
+  // from div_lanes on all lanes at once, a zero divisor lane replaced by 1.
   __device__ static __forceinline__ uint32_t word_checked(uint32_t a, uint32_t b, uint32_t& o) {
     constexpr uint32_t M = (1u << W) - 1;
-    uint32_t bad = 0;
-    if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI)
-      bad = W == 8 ? __vcmpgeu4(b, 0x08080808u) : __vcmpgeu2(b, 0x00100010u);
-    if constexpr (OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI)
-      bad = W == 8 ? __vcmpeq4(b, 0u) : __vcmpeq2(b, 0u);
-    if constexpr (OP == DCF_DIVSI)
-      bad |= W == 8 ? (__vcmpeq4(a, 0x80808080u) & __vcmpeq4(b, 0xFFFFFFFFu))
-                    : (__vcmpeq2(a, 0x80008000u) & __vcmpeq2(b, 0xFFFFFFFFu));
-    uint32_t r = 0;
+    if constexpr (OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI) {
+      const uint32_t zero = W == 8 ? __vcmpeq4(b, 0u) : __vcmpeq2(b, 0u);
+      uint32_t bad = zero;
+      if constexpr (OP == DCF_DIVSI)
+        bad |= W == 8 ? (__vcmpeq4(a, 0x80808080u) & __vcmpeq4(b, 0xFFFFFFFFu))
+                      : (__vcmpeq2(a, 0x80008000u) & __vcmpeq2(b, 0xFFFFFFFFu));
+      o = div_lanes<OP, W>(a, b | (zero & (W == 8 ? 0x01010101u : 0x00010001u)));
+      return bad;
+    } else {
+      uint32_t bad = 0;
+      if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI)
+        bad = W == 8 ? __vcmpgeu4(b, 0x08080808u) : __vcmpgeu2(b, 0x00100010u);
+      uint32_t r = 0;
 #pragma unroll
-    for (int k = 0; k < 32 / W; k++) {
-      const uint32_t x = (a >> (W * k)) & M;
-      uint32_t y = (b >> (W * k)) & M;
-      if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI) y &= W - 1;
-      if constexpr (OP == DCF_DIVSI || OP == DCF_DIVUI || OP == DCF_REMSI || OP == DCF_REMUI) y = y ? y : 1;
-      const int32_t sx = (int32_t)(x << (32 - W)) >> (32 - W), sy = (int32_t)(y << (32 - W)) >> (32 - W);
-      uint32_t z;
-      if constexpr (OP == DCF_MULI) z = x * y;
-      else if constexpr (OP == DCF_SHLI) z = x << y;
-      else if constexpr (OP == DCF_SHRUI) z = x >> y;
-      else if constexpr (OP == DCF_SHRSI) z = (uint32_t)(sx >> y);
-      else if constexpr (OP == DCF_DIVUI || OP == DCF_REMUI) {
-        const uint32_t q = udiv_small<W == 8 ? 2 : 3>(x, y);
-        z = OP == DCF_DIVUI ? q : x - q * y;
-      } else {
-        const uint32_t ax = (uint32_t)(sx < 0 ? -sx : sx), ay = (uint32_t)(sy < 0 ? -sy : sy);
-        const uint32_t qm = udiv_small<W == 8 ? 2 : 3>(ax, ay);
-        const int32_t q = ((sx ^ sy) < 0) ? -(int32_t)qm : (int32_t)qm;
-        z = (uint32_t)(OP == DCF_DIVSI ? q : sx - q * sy);
+      for (int k = 0; k < 32 / W; k++) {
+        const uint32_t x = (a >> (W * k)) & M;
+        uint32_t y = (b >> (W * k)) & M;
+        if constexpr (OP == DCF_SHLI || OP == DCF_SHRUI || OP == DCF_SHRSI) y &= W - 1;
+        uint32_t z;
+        if constexpr (OP == DCF_MULI) z = x * y;
+        else if constexpr (OP == DCF_SHLI) z = x << y;
+        else if constexpr (OP == DCF_SHRUI) z = x >> y;
+        else z = (uint32_t)((int32_t)(x << (32 - W)) >> (32 - W) >> y);
+        r |= (z & M) << (W * k);
       }
-      r |= (z & M) << (W * k);
+      o = r;
+      return bad;
     }
-    o = r;
-    return bad;
   }
   __device__ static __forceinline__ uint32_t word(uint32_t a, uint32_t b) {
     if constexpr (OP == DCF_ANDI) return a & b;

@@ -357,3 +357,37 @@ def test_i8_lanes_exhaustive_and_i16_edges(op, dcf, oracle):
     if op == "divsi":
         b = np.where((a == 0x8000) & (b == 0xFFFF), np.uint16(1), b)
     same(dcf.binary(op, "i16", a, b), oracle.binary(op, "i16", a, b), a.size)
+
+
+def i16_division_boundaries():
+    """Every i16 divisor with the dividends next to its multiples (n d - 1,
+    n d, n d + 1), where a quotient taken from a reciprocal is first wrong,
+    as unsigned lanes and as signed lanes of all four sign combinations."""
+    xs, ys = [], []
+    for d in range(1, 65536):
+        m = np.arange(0, 65536 // d + 2, dtype=np.int64) * d
+        m = np.concatenate([m - 1, m, m + 1, [0, 1, 32767, 32768, 65535]])
+        m = m[(m >= 0) & (m < 65536)]
+        xs.append(m)
+        ys.append(np.full(m.size, d))
+    for d in range(1, 32769):
+        m = np.arange(0, 32768 // d + 2, dtype=np.int64) * d
+        m = np.concatenate([m - 1, m, m + 1])
+        m = m[(m >= 0) & (m <= 32768)]
+        for sd in (1, -1) if d < 32768 else (-1,):
+            for sx in (1, -1):
+                v = sx * m
+                v = v[(v >= -32768) & (v <= 32767)]
+                xs.append(v & 0xFFFF)
+                ys.append(np.full(v.size, (sd * d) & 0xFFFF))
+    return np.concatenate(xs).astype(np.uint16), np.concatenate(ys).astype(np.uint16)
+
+
+@pytest.mark.parametrize("op", ["divsi", "divui", "remsi", "remui"])
+def test_i16_lane_division_boundaries(op, dcf, oracle):
+    a, b = i16_division_boundaries()
+    if op == "divsi":
+        b = np.where((a == 0x8000) & (b == 0xFFFF), np.uint16(1), b)
+    for shift in (0, 1):  # every pair in both lanes of its word
+        a2, b2 = np.roll(a, shift).copy(), np.roll(b, shift).copy()
+        same(dcf.binary(op, "i16", a2, b2), oracle.binary(op, "i16", a2, b2), a2.size)
